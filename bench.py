@@ -1,0 +1,497 @@
+#!/usr/bin/env python
+"""bench.py -- device-timed throughput of the B200 attention (and MLP) hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
+        bench.py --gpus N ...
+    python bench.py --impl reference ...     # the CPU implementation of the path
+
+A "step" is one pass of the hot path over one batch: one attention forward
+over this rank's (batch, head) shard (or one MLP block for cfg3).  Inputs are
+generated on each GPU from the seed before timing, per (batch, head) pair, so
+any sharding reproduces the same tensors.  Timing follows the reference's
+method (CUDA events around the kernel loop after warm-up, ``bench.py:49-74``
+of the reference) with a barrier + synchronize on both sides and the maximum
+over ranks.  Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from cs348k_fast_attention_grammar_b200.inputs import (ATTN_CONFIGS, MLP_CONFIGS,  # noqa: E402
+                                                       make_mlp, make_qkv, pair_tensor)
+from cs348k_fast_attention_grammar_b200.parallel import (gather_shards,  # noqa: E402
+                                                         reduce_error_stats, shard_range,
+                                                         verify_pairs)
+
+METRIC = "attn fwd TFLOP/s per GPU, % of bf16 tensor peak; box TFLOP/s at 1/2/4/8 GPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--config", choices=sorted(list(ATTN_CONFIGS) + list(MLP_CONFIGS)),
+                    default="cfg2")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--verify-pairs", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args(argv)
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", 0.0)),
+                "source": "measured"}
+    except Exception:
+        return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def load_traffic(config: str):
+    """Per-launch DRAM bytes (read + write) of the dominant kernel, from the
+    committed ncu summary profiles/ncu_traffic.txt (``<config> <bytes>`` lines)."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and parts[0] == config:
+                    return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML (the library
+    nvidia-smi reads) every 20 ms while the timed region runs."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting", 0x10: "sync_boost"}
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            if not uuid.startswith("GPU-"):
+                uuid = "GPU-" + uuid
+            self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._nvml = pynvml
+        except Exception as e:  # noqa: BLE001
+            self.error = f"nvml unavailable: {e}"
+
+    def _reasons_now(self):
+        n = self._nvml
+        fn = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            getattr(n, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        return fn(self._h)
+
+    def _run(self):
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM))
+                mask = self._reasons_now()
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.02)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if self._nvml is None:
+            return {"error": getattr(self, "error", "nvml unavailable")}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+def timed_loop(fn, steps: int, world: int, device) -> float:
+    """Mean ms per step over ``steps`` calls, CUDA events on the current
+    stream, barrier + synchronize on both sides, max over ranks."""
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        fn()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+        dist.barrier()
+    return ms
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def attn_flops(cfg, pairs=None) -> float:
+    import oracle  # only for the FLOP convention of the reference (old/benchmark.py:131)
+    n = cfg["B"] * cfg["H"] if pairs is None else pairs
+    return float(oracle.attention_flops(1, n, cfg["S"], cfg["D"], cfg["causal"]))
+
+
+def cpu_attention_sample(cfg, seconds: float, max_pairs: int = 10_000):
+    """Time the CPU restatement of the naive path (oracle.naive_torch_pair) on
+    seeded pairs until ``seconds`` elapse; returns (TFLOP/s, pairs, seconds)."""
+    import oracle
+    torch.set_num_threads(host_cores())
+    done, t_total = 0, 0.0
+    p = 0
+    while done < max_pairs and (t_total < seconds or done == 0):
+        q, k, v = (pair_tensor(cfg["seed"], n, p, cfg["S"], cfg["D"], cfg["amp"], "cpu",
+                               torch.float32) for n in ("q", "k", "v"))
+        t0 = time.perf_counter()
+        oracle.naive_torch_pair(q, k, v, causal=cfg["causal"])
+        t_total += time.perf_counter() - t0
+        done += 1
+        p += 1
+    return attn_flops(cfg, done) / t_total / 1e12, done, t_total
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the CPU implementation of the path on this host
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    if args.config in MLP_CONFIGS:
+        return run_reference_mlp(args)
+    import oracle
+    cfg = ATTN_CONFIGS[args.config]
+    torch.set_num_threads(host_cores())
+    q, k, v = (pair_tensor(cfg["seed"], n, 0, cfg["S"], cfg["D"], cfg["amp"], "cpu",
+                           torch.float32) for n in ("q", "k", "v"))
+    for _ in range(args.warmup):
+        oracle.naive_torch_pair(q, k, v, causal=cfg["causal"])
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.naive_torch_pair(q, k, v, causal=cfg["causal"])
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(times)
+    value = attn_flops(cfg, 1) / (ms * 1e-3) / 1e12
+    sample = (f"one (batch, head) pair per step (S={cfg['S']}, D={cfg['D']}, "
+              f"causal={cfg['causal']}) of the {args.config} workload; pairs are independent")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,1) per pair", "config": workload_config(args, cfg),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample, "cpu": cpu_model(),
+                         "what": "oracle.naive_torch_pair: correct restatement of "
+                                 "pytorch-naive.py:41-63 in fp32 torch"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_reference_mlp(args):
+    import oracle
+    cfg = MLP_CONFIGS[args.config]
+    torch.set_num_threads(host_cores())
+    rows = 256
+    x, w1, w2 = (t.float() for t in make_mlp(dict(cfg, M=rows), "cpu"))
+    fn = lambda: torch.nn.functional.gelu(x @ w1, approximate="tanh") @ w2  # noqa: E731
+    for _ in range(args.warmup):
+        fn()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(times)
+    value = oracle.mlp_flops(rows, cfg["K"], cfg["N"]) / (ms * 1e-3) / 1e12
+    line = {"impl": "reference", "metric": "MLP block TFLOP/s", "value": value,
+            "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": f"{args.config} MLP, {rows} rows"},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": f"{rows} rows of X per step"},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args, cfg):
+    S, D = cfg["S"], cfg["D"]
+    qkv_bytes = 3 * cfg["B"] * cfg["H"] * S * D * 2
+    return {"workload": (f"{args.config}: attention forward {'causal' if cfg['causal'] else 'non-causal'}"
+                         f" bf16 B={cfg['B']} H={cfg['H']} S={S} D={D}"),
+            "B": cfg["B"], "H": cfg["H"], "S": S, "D": D, "causal": cfg["causal"],
+            "seed": cfg["seed"], "parallelism": f"dp over batch*head x {args.gpus}",
+            "l2": (f"inputs larger than L2 ({qkv_bytes / 2**20:.0f} MiB of Q/K/V per step "
+                   f"> 126 MiB), no flush") if qkv_bytes > L2_BYTES else
+                  "L2 not flushed (inputs smaller than L2)"}
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    import cs348k_fast_attention_grammar_b200 as fab
+    fab.load()
+    if args.config in MLP_CONFIGS:
+        line = bench_mlp(args, fab, device, world, rank)
+    else:
+        line = bench_attention(args, fab, device, world, rank)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def roofline(achieved_tflops, peaks, traffic):
+    peak = peaks["bf16_tflops"]
+    return {"bound": "tensor", "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved_tflops / peak, "traffic": traffic,
+            "peak_source": f"{peaks['source']} (bf16 dense burst, cuBLAS)"}
+
+
+def bench_attention(args, fab, device, world, rank):
+    cfg = ATTN_CONFIGS[args.config]
+    num_pairs = cfg["B"] * cfg["H"]
+    pairs = shard_range(num_pairs, world, rank)
+    q, k, v = make_qkv(cfg, pairs, device)
+    o = torch.empty_like(q)
+    step = lambda: fab.attention(q, k, v, causal=cfg["causal"], out=o)  # noqa: E731
+    for _ in range(max(args.warmup, 0)):
+        step()
+    torch.cuda.synchronize()
+    with ClockSampler(local_index(device)) as clk:
+        ms = timed_loop(step, args.steps, world, device)
+    flops_total = attn_flops(cfg)
+    value = flops_total / (ms * 1e-3) / 1e12
+    flops_local = attn_flops(cfg, len(pairs))
+    achieved = flops_local / (ms * 1e-3) / 1e12
+    peaks = load_peaks()
+
+    # verification: seeded subset of pairs vs a torch fp32 reference, per owner
+    vp = verify_pairs(num_pairs, args.verify_pairs)
+    max_abs, sum_abs, count = 0.0, 0.0, 0
+    for p in vp:
+        if p in pairs:
+            i = p - pairs.start
+            ref = torch_ref_pair(q[0, i], k[0, i], v[0, i], cfg["causal"])
+            d = (o[0, i].float() - ref).abs()
+            max_abs = max(max_abs, d.max().item())
+            sum_abs += d.sum().item()
+            count += d.numel()
+    verify = reduce_error_stats(max_abs, sum_abs, count, device)
+    verify.update({"pairs": len(vp), "ok": verify["max_abs"] <= 2e-2 and verify["mean_abs"] <= 2e-3,
+                   "reference": "torch fp32 on GPU, per pair"})
+
+    gather_ms = None
+    if world > 1:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        full = gather_shards(o, world, rank, num_pairs)
+        torch.cuda.synchronize()
+        gather_ms = 1e3 * (time.perf_counter() - t0)
+        del full
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = attention_e2e(args, fab, cfg, q, k, v, world, device, flops_total)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, npairs_cpu, secs = cpu_attention_sample(cfg, args.cpu_seconds)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{npairs_cpu} (batch, head) pairs of {args.config} in {secs:.1f} s "
+                         "(pairs are independent; throughput scales linearly)",
+               "cpu": cpu_model(),
+               "what": "oracle.naive_torch_pair: correct restatement of pytorch-naive.py:41-63"}
+    return {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": f"synthetic: seeded N(0,1)*{cfg['amp']} per (batch, head) pair (Philox), bf16",
+        "config": workload_config(args, cfg),
+        "per_gpu_tflops": value / world,
+        "pct_of_peak": 100.0 * achieved / peaks["bf16_tflops"],
+        "roofline": roofline(achieved, peaks, load_traffic(args.config)),
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "verify": verify,
+        "gather_ms": gather_ms,
+        "flops_per_step": flops_total,
+        "flop_convention": "4*B*H*S^2*D, halved when causal (old/benchmark.py:131)",
+    }
+
+
+def local_index(device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
+def torch_ref_pair(q, k, v, causal, row_chunk=2048):
+    qf, kf, vf = q.float(), k.float(), v.float()
+    S, D = qf.shape
+    out = torch.empty_like(qf)
+    for r0 in range(0, S, row_chunk):
+        s = (qf[r0:r0 + row_chunk] @ kf.t()) / math.sqrt(D)
+        if causal:
+            rows = torch.arange(r0, min(S, r0 + row_chunk), device=q.device)[:, None]
+            s = s.masked_fill(torch.arange(S, device=q.device)[None, :] > rows, float("-inf"))
+        out[r0:r0 + row_chunk] = torch.softmax(s, dim=-1) @ vf
+    return out
+
+
+def attention_e2e(args, fab, cfg, q, k, v, world, device, flops_total):
+    """Same metric through the public API fed from pinned host buffers:
+    H2D of this rank's Q/K/V, the kernel, D2H of O, every step."""
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    oh = torch.empty(q.shape, dtype=torch.bfloat16, pin_memory=True)
+    ws = {}
+    step = lambda: fab.attention_from_host(qh, kh, vh, causal=cfg["causal"], out=oh,  # noqa
+                                           device=device, workspace=ws)
+    step()
+    torch.cuda.synchronize()
+    steps = max(1, args.e2e_steps)
+    ms = timed_loop(step, steps, world, device)
+    return {"value": flops_total / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "steps": steps, "h2d_bytes_per_step": 3 * q.numel() * 2 * world,
+            "d2h_bytes_per_step": q.numel() * 2 * world,
+            "path": "attention_from_host (pinned host -> device -> host)"}
+
+
+def bench_mlp(args, fab, device, world, rank):
+    import oracle
+    cfg = MLP_CONFIGS[args.config]
+    x, w1, w2 = make_mlp(cfg, device)
+    M, K, N = cfg["M"], cfg["K"], cfg["N"]
+    hidden = torch.empty((M, N), dtype=torch.bfloat16, device=device)
+    y = torch.empty((M, K), dtype=torch.bfloat16, device=device)
+    step = lambda: fab.mlp(x, w1, w2, act="gelu_tanh", hidden=hidden, out=y)  # noqa: E731
+    for _ in range(max(args.warmup, 0)):
+        step()
+    with ClockSampler(local_index(device)) as clk:
+        ms = timed_loop(step, args.steps, world, device)
+    # per-GEMM durations for the roofline of the dominant kernel
+    stream = torch.cuda.current_stream(device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    g1, g2 = [], []
+    for _ in range(5):
+        ev[0].record(stream)
+        fab.gemm_act(x, w1, act="gelu_tanh", out=hidden)
+        ev[1].record(stream)
+        fab.gemm_act(hidden, w2, act="none", out=y)
+        ev[2].record(stream)
+        torch.cuda.synchronize()
+        g1.append(ev[0].elapsed_time(ev[1]))
+        g2.append(ev[1].elapsed_time(ev[2]))
+    gemm_flops = 2.0 * M * K * N
+    t1, t2 = statistics.mean(g1), statistics.mean(g2)
+    dom = max(t1, t2)
+    flops = float(oracle.mlp_flops(M, K, N)) * world
+    value = flops / (ms * 1e-3) / 1e12
+    peaks = load_peaks()
+    return {"metric": "MLP block TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: X~N(0,1), W~N(0,1/fan_in), bf16",
+            "config": {"workload": f"{args.config}: Y=gelu_tanh(X W1) W2, M={M} K={K} N={N}",
+                       "parallelism": f"replicas x {world}",
+                       "l2": "inputs larger than L2 (X 64 MiB + W1 128 MiB + W2 128 MiB)"},
+            "pct_of_peak": 100.0 * value / world / peaks["bf16_tflops"],
+            "roofline": roofline(gemm_flops / (dom * 1e-3) / 1e12, peaks,
+                                 load_traffic(args.config)),
+            "gemm_ms": {"gemm1_gelu": t1, "gemm2": t2},
+            "gpu_launches": 2 * args.steps, "clocks": clk.summary(), "cpu_baseline": None,
+            "e2e": None}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,27 @@
+"""B200-native (sm_100a) fused attention forward and GEMM-GELU-GEMM MLP.
+
+Public operators (all run the hand-written kernels of ``libfa_b200.so``
+through its C ABI, ``include/fa_b200.h``; there is no fallback path):
+
+    attention(q, k, v, causal=False, scale=None, out=None)   # [B, H, S, D] bf16
+    attention_bshd(q, k, v, causal=False)                    # (B, S, H, D) layout
+    attention_from_host(q, k, v, causal=False, ...)          # pinned host tensors
+    mlp(x, w1, w2, act="gelu_tanh")                          # act(x@w1)@w2
+    gemm_act(a, b, act="none")                               # act(a@b)
+
+``kernel_module`` exposes the reference's ``fn(KT, Q, V)`` + ``KERNEL_META``
+protocol; ``parallel`` holds the batch x head sharding used by ``bench.py``.
+"""
+
+from ._lib import FaError, lib_path, load  # noqa: F401
+from .operators import (  # noqa: F401
+    attention,
+    attention_bshd,
+    attention_from_host,
+    device_status,
+    gemm_act,
+    mlp,
+)
+
+__all__ = ["attention", "attention_bshd", "attention_from_host", "mlp", "gemm_act",
+           "device_status", "FaError", "load", "lib_path"]

@@ -1,0 +1,428 @@
+// Fused attention forward for sm_100a (B200):
+//     O = softmax(Q K^T * scale [+ causal mask]) V        per (batch, head)
+//
+// Replaces the reference's six-launch cuTile pipeline (Ss, mx, e, sm, P, O
+// kernels of runs/attn_full/kernels/best_it24.py:17-99, i.e. the 8 stages of
+// run_attention_search.py:49-85) with one kernel that keeps S, P and O on
+// chip (tensor memory) and streams K/V once per CTA.
+//
+// Work unit (one CTA): one (batch, head) pair and 256 query rows, held as two
+// 128-row Q tiles that ping-pong between the tensor cores and the softmax
+// warps.  Warp roles (12 warps, 384 threads):
+//   warps 0-3  softmax for Q tile 0 (thread = one query row = one TMEM lane)
+//   warps 4-7  softmax for Q tile 1
+//   warp  8    TMA producer: Q tiles once, then K_j / V_j 128-key blocks into
+//              a ring of shared-memory slots
+//   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 10-11 idle (keep the register budget of the softmax warps)
+// Tensor memory (512 columns x 128 lanes x 32 bit):
+//   S_t at columns [128 t, 128 t + 128)  fp32 scores of tile t
+//   P_t aliases the first 64 columns of S_t (128 bf16 probabilities per row)
+//   O_t at columns [256 + D t, 256 + D t + D)  fp32 output accumulator
+// Per KV block j the MMA warp issues, in this order,
+//   O_0 += P_0(j-1) V_{j-1};  S_0 = Q_0 K_j^T;  O_1 += P_1(j-1) V_{j-1};  S_1 = Q_1 K_j^T
+// so "S_t(j) complete" implies "O_t holds all blocks < j", which is when the
+// softmax warps may rescale O_t in place.
+// Online softmax (exp2 domain, log2(e) folded into the scale): the running
+// row maximum is only raised when a block's maximum exceeds it by more than
+// 8 (a factor 256), which keeps O_t rescales rare; the final O / l is exact
+// for any reference maximum.
+#include <cuda_bf16.h>
+
+#include "fa_internal.h"
+#include "sm100_ptx.cuh"
+#include "sm100_tmem_wide.cuh"
+
+namespace fa {
+namespace {
+
+constexpr int kBM = 128;          // query rows per tile (= TMEM lanes)
+constexpr int kBN = 128;          // keys per KV block
+constexpr int kThreads = 384;
+constexpr float kRescaleThreshold = 8.0f;
+
+template <int D>
+struct AttnCfg {
+  static constexpr int kTileBytes = kBM * D * 2;          // one 128 x D bf16 tile
+  static constexpr int kStages = (D == 128) ? 4 : 8;      // K/V ring slots
+  static constexpr int kQOff = 0;
+  static constexpr int kKVOff = 2 * kTileBytes;
+  static constexpr int kBarOff = kKVOff + kStages * kTileBytes;
+  // q_full, kv_full[kStages], kv_empty[kStages], s_full[2], p_full[2],
+  // o_full[2], drain
+  static constexpr int kNumBars = 1 + 2 * kStages + 7;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem base, abort flag
+  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + alignment slack
+  // TMEM column of S_t (P_t aliases its first 64 columns) and of O_t.
+  __device__ static constexpr uint32_t col_s(int t) { return 128u * t; }
+  __device__ static constexpr uint32_t col_o(int t) { return 256u + D * t; }
+};
+
+struct AttnParams {
+  int B, H, S;
+  int n_units_per_head;   // ceil(S / 256)
+  int nkv;                // ceil(S / 128)
+  float scale_log2;       // scale * log2(e)
+  __nv_bfloat16* o;
+  int64_t o_sb, o_sh, o_ss;
+  int* status;
+};
+
+// Bounded drain wait used only on the abort path: returns when the phase
+// completes or after a short limit, ignoring the abort flag.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > 50ull * 1000ull * 1000ull) return;
+  }
+}
+
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                    const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using C = AttnCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sQ = base + C::kQOff;
+  const uint32_t sKV = base + C::kKVOff;
+  const uint32_t bars = base + C::kBarOff;
+  const uint32_t bar_q = bars;
+  auto bar_kv_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto bar_kv_empty = [&](int s) { return bars + 8u * (1 + C::kStages + s); };
+  auto bar_s_full = [&](int t) { return bars + 8u * (1 + 2 * C::kStages + t); };
+  auto bar_p_full = [&](int t) { return bars + 8u * (3 + 2 * C::kStages + t); };
+  auto bar_o_full = [&](int t) { return bars + 8u * (5 + 2 * C::kStages + t); };
+  const uint32_t bar_drain = bars + 8u * (7 + 2 * C::kStages);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + C::kMiscOff + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---- work unit: (batch, head) major, longest causal unit first ----------
+  const int bh = blockIdx.x / p.n_units_per_head;
+  int qu = blockIdx.x - bh * p.n_units_per_head;
+  if (CAUSAL) qu = p.n_units_per_head - 1 - qu;
+  const int b = bh / p.H;
+  const int h = bh - b * p.H;
+  const int q0 = qu * 2 * kBM;
+  int nt[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qs = q0 + t * kBM;
+    if (qs >= p.S) nt[t] = 0;
+    else if (CAUSAL) nt[t] = min(p.nkv, qs / kBN + 1);
+    else nt[t] = p.nkv;
+  }
+  const int n = max(nt[0], nt[1]);
+
+  // ---- setup ----------------------------------------------------------------
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar_kv_full(s), 1);
+      mbar_init(bar_kv_empty(s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar_s_full(t), 1);
+      mbar_init(bar_p_full(t), kBM);
+      mbar_init(bar_o_full(t), 1);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // =================== TMA producer ===================
+    if (elect_one()) {
+      const uint64_t pol_q = l2_policy_evict_first();
+      const uint64_t pol_kv = l2_policy_evict_last();
+      mbar_arrive_expect_tx(bar_q, 2 * C::kTileBytes);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int dk = 0; dk < D / 64; ++dk)
+          tma_load_4d(sQ + t * C::kTileBytes + dk * 16384, &tmQ, bar_q, dk * 64, q0 + t * kBM,
+                      h, b, pol_q);
+      int issued = 0;
+      for (int i = 0; i < 2 * n; ++i) {
+        const int s = i % C::kStages;
+        const uint32_t ph = (i / C::kStages) & 1;
+        if (!mbar_wait(bar_kv_empty(s), ph ^ 1u, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(bar_kv_full(s), C::kTileBytes);
+        const void* map = (i & 1) ? static_cast<const void*>(&tmV)
+                                  : static_cast<const void*>(&tmK);
+        const int j = i >> 1;
+#pragma unroll
+        for (int dk = 0; dk < D / 64; ++dk)
+          tma_load_4d(sKV + s * C::kTileBytes + dk * 16384, map, bar_kv_full(s), dk * 64,
+                      j * kBN, h, b, pol_kv);
+        ++issued;
+      }
+      if (*abort_flag) {
+        // Let the copies already in flight land before the CTA exits.
+        drain_wait(bar_q, 0);
+        for (int i = max(0, issued - C::kStages); i < issued; ++i)
+          drain_wait(bar_kv_full(i % C::kStages), (i / C::kStages) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    // =================== MMA issuer ===================
+    if (elect_one()) {
+      constexpr uint32_t kIdQK = idesc_bf16_f32(kBM, kBN, false, false);
+      constexpr uint32_t kIdPV = idesc_bf16_f32(kBM, D, false, true);
+      bool ok = mbar_wait(bar_q, 0, abort_flag, p.status);
+      tc_fence_after();
+      int vslot = 0;
+      for (int j = 0; ok && j <= n; ++j) {
+        int kslot = 0;
+        if (j < n) {
+          const int i = 2 * j;
+          kslot = i % C::kStages;
+          if (!mbar_wait(bar_kv_full(kslot), (i / C::kStages) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (j >= 1 && j - 1 < nt[t]) {
+            // O_t += P_t(j-1) V_{j-1}: A = P from TMEM (8 columns per K=16 step),
+            // B = V tile, MN-major (d contiguous), 64-wide d atoms 16 KiB apart.
+            if (!mbar_wait(bar_p_full(t), (j - 1) & 1, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t vbase = sKV + vslot * C::kTileBytes;
+#pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk) {
+              const uint64_t bdesc = sdesc_sw128(vbase + kk * 2048, 16384, 1024);
+              mma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8, bdesc, kIdPV,
+                     (j - 1 > 0 || kk > 0) ? 1u : 0u);
+            }
+            if (j - 1 == nt[t] - 1) mma_commit(bar_o_full(t));
+          }
+          if (j < nt[t]) {
+            // S_t = Q_t K_j^T: both K-major, 64-element swizzle atoms 16 KiB apart.
+            const uint32_t qbase = sQ + t * C::kTileBytes;
+            const uint32_t kbase = sKV + kslot * C::kTileBytes;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+              mma_ss(tmem + C::col_s(t), sdesc_sw128(qbase + off, 16, 1024),
+                     sdesc_sw128(kbase + off, 16, 1024), kIdQK, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(bar_s_full(t));
+          }
+        }
+        if (!ok) break;
+        if (j >= 1) mma_commit(bar_kv_empty(vslot));      // V_{j-1} consumed
+        if (j < n) {
+          mma_commit(bar_kv_empty(kslot));                // K_j consumed
+          const int i = 2 * j + 1;
+          vslot = i % C::kStages;
+          if (!mbar_wait(bar_kv_full(vslot), (i / C::kStages) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+      }
+      // Every issued MMA (and its commit arrivals) completes before teardown.
+      mma_commit(bar_drain);
+      drain_wait(bar_drain, 0);
+    }
+    __syncwarp();
+  } else if (warp < 8) {
+    // =================== softmax / correction / epilogue ===================
+    const int t = warp >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const int qi = q0 + t * kBM + row;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_off + C::col_s(t);
+    const uint32_t tO = tmem + lane_off + C::col_o(t);
+    const float sl2 = p.scale_log2;
+    float m_ref = -INFINITY;   // reference row max, already scaled (log2 domain)
+    float l = 0.f;             // running row sum of exp2(s * sl2 - m_ref)
+    bool ok = true;
+    const int q_tile0 = q0 + t * kBM;
+    for (int j = 0; j < nt[t]; ++j) {
+      if (!mbar_wait(bar_s_full(t), j & 1, abort_flag, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[128];
+      tmem_ld128_wait(tS, sr);
+      const int k0 = j * kBN;
+      const bool need_mask = (k0 + kBN > p.S) || (CAUSAL && (k0 + kBN - 1 > q_tile0));
+      if (need_mask) {
+        const int lim = CAUSAL ? min(qi + 1, p.S) : p.S;   // keys [0, lim) visible
+#pragma unroll
+        for (int c = 0; c < kBN; ++c)
+          if (k0 + c >= lim) sr[c] = __float_as_uint(-INFINITY);
+      }
+      float mx = __uint_as_float(sr[0]);
+#pragma unroll
+      for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      const float m_blk = mx * sl2;
+      const float m_new = fmaxf(m_ref, m_blk);
+      const bool need = (m_new - m_ref) > kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_use = need ? m_new : m_ref;
+        const float alpha = ex2_approx(m_ref - m_use);   // 1 if unchanged, 0 at start
+        if (j > 0) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32_wait(tO + c * 32, o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + c * 32, o);
+          }
+        }
+        l *= alpha;
+        m_ref = m_use;
+      }
+      const float neg_m = -m_ref;
+      float rs0 = 0.f, rs1 = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * c]), sl2, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * c + 1]), sl2, neg_m));
+        rs0 += p0;
+        rs1 += p1;
+        pk[c] = pack_bf16x2(p0, p1);
+      }
+      l += rs0 + rs1;
+      tmem_st64(tS, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar_p_full(t));
+    }
+    if (ok && nt[t] > 0 && mbar_wait(bar_o_full(t), 0, abort_flag, p.status)) {
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      __nv_bfloat16* orow = p.o + static_cast<int64_t>(b) * p.o_sb +
+                            static_cast<int64_t>(h) * p.o_sh + static_cast<int64_t>(qi) * p.o_ss;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32_wait(tO + c * 32, o);
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          w[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv_l,
+                             __uint_as_float(o[2 * e + 1]) * inv_l);
+        if (qi < p.S) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+          dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+        }
+      }
+    }
+  }
+
+  // ---- teardown ---------------------------------------------------------------
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D, bool CAUSAL>
+int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                const AttnParams& prm, int grid, cudaStream_t stream) {
+  using C = AttnCfg<D>;
+  auto kern = attn_fwd_kernel<D, CAUSAL>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  int rc = FA_OK;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FA_ERR_CUDA;
+  if (!attr_set[dev]) {
+    rc = prepare_device(reinterpret_cast<const void*>(kern), C::kSmemBytes, &dev);
+    if (rc != FA_OK) return rc;
+    attr_set[dev] = true;
+  }
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(mq, mk, mv, prm);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+}  // namespace
+}  // namespace fa
+
+extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int H,
+                           int S, int D, const int64_t* st, int causal, float scale,
+                           void* stream) {
+  using namespace fa;
+  if (!q || !k || !v || !o || !st) return FA_ERR_NULL;
+  if (B <= 0 || H <= 0 || S <= 0) return FA_ERR_SHAPE;
+  if (D != 64 && D != 128) return FA_ERR_HEAD_DIM;
+  const int64_t units = static_cast<int64_t>(B) * H * ((S + 2 * kBM - 1) / (2 * kBM));
+  if (units > 0x7fffffffLL) return FA_ERR_SHAPE;
+  for (int t = 0; t < 4; ++t) {
+    if (st[4 * t + 3] != 1) return FA_ERR_STRIDE;
+    for (int i = 0; i < 3; ++i)
+      if (st[4 * t + i] <= 0 || (st[4 * t + i] % 8) != 0) return FA_ERR_ALIGN;
+  }
+  const void* ptrs[4] = {q, k, v, o};
+  for (int t = 0; t < 4; ++t)
+    if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 != 0) return FA_ERR_ALIGN;
+
+  int dev = 0;
+  int rc = prepare_device(nullptr, 0, &dev);
+  if (rc != FA_OK) return rc;
+  CUtensorMap mq, mk, mv;
+  if ((rc = make_tmap_bhsd(&mq, q, B, H, S, D, st[0], st[1], st[2], kBM)) != FA_OK) return rc;
+  if ((rc = make_tmap_bhsd(&mk, k, B, H, S, D, st[4], st[5], st[6], kBN)) != FA_OK) return rc;
+  if ((rc = make_tmap_bhsd(&mv, v, B, H, S, D, st[8], st[9], st[10], kBN)) != FA_OK) return rc;
+
+  AttnParams prm;
+  prm.B = B;
+  prm.H = H;
+  prm.S = S;
+  prm.n_units_per_head = (S + 2 * kBM - 1) / (2 * kBM);
+  prm.nkv = (S + kBN - 1) / kBN;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.o = static_cast<__nv_bfloat16*>(o);
+  prm.o_sb = st[12];
+  prm.o_sh = st[13];
+  prm.o_ss = st[14];
+  prm.status = device_status_ptr();
+  if (prm.status == nullptr) return FA_ERR_CUDA;
+  const int grid = static_cast<int>(units);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (D == 64)
+    return causal ? launch_attn<64, true>(mq, mk, mv, prm, grid, s)
+                  : launch_attn<64, false>(mq, mk, mv, prm, grid, s);
+  return causal ? launch_attn<128, true>(mq, mk, mv, prm, grid, s)
+                : launch_attn<128, false>(mq, mk, mv, prm, grid, s);
+}

@@ -1,0 +1,305 @@
+// GEMM with fused pointwise epilogue for sm_100a (B200):
+//     C[M, N] = act(A[M, K] @ B[K, N])       bf16 in/out, fp32 accumulate
+// and the MLP block built from two of them:
+//     hidden = act(X @ W1);  Y = hidden @ W2
+// (run_mlp_search.py:58-69: h = X@W1, a = act(h), y = a@W2; the reference
+// lowers each matmul to a ct.mma K-loop, grammar/kernel_ast.py:207-211, and
+// the activation to its own elementwise kernel -- here it is the epilogue).
+//
+// Persistent kernel, one CTA per SM, 128 x 256 output tiles, K step 64:
+//   warp 0      TMA producer: A tile 128 x 64 (K-major), B tile 64 x 256
+//               (N contiguous = MN-major operand) into a 4-stage ring
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//               (M=128, N=256, K=16 per instruction, fp32 accumulator in TMEM)
+//   warps 2-5   epilogue: TMEM -> registers, activation, bf16, global store;
+//               two accumulators (TMEM columns 0-255 and 256-511) let the
+//               epilogue of tile i overlap the main loop of tile i+1.
+#include <cuda_bf16.h>
+
+#include "fa_internal.h"
+#include "sm100_ptx.cuh"
+#include "sm100_tmem_wide.cuh"
+
+namespace fa {
+namespace {
+
+constexpr int kGBM = 128;
+constexpr int kGBN = 256;
+constexpr int kGBK = 64;
+constexpr int kGStages = 4;
+constexpr int kGThreads = 192;
+constexpr int kABytes = kGBM * kGBK * 2;            // 16 KiB
+constexpr int kBBytes = kGBK * kGBN * 2;            // 32 KiB (4 atoms of 64 x 64)
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kGBarOff = kGStages * kStageBytes;
+constexpr int kGNumBars = 2 * kGStages + 4 + 1;     // full, empty, acc_full[2], acc_empty[2], drain
+constexpr int kGMiscOff = kGBarOff + kGNumBars * 8;
+constexpr int kGSmemBytes = kGMiscOff + 16 + 1024;
+constexpr int kGroupM = 8;                          // tile raster: 8 M-tiles per band
+
+struct GemmParams {
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles;
+  int act;
+  __nv_bfloat16* c;
+  int64_t ldc;
+  int* status;
+};
+
+__device__ __forceinline__ void gemm_drain_wait(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > 50ull * 1000ull * 1000ull) return;
+  }
+}
+
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& tm, int& tn) {
+  const int per_group = kGroupM * p.tiles_n;
+  const int g = tile / per_group;
+  const int first_m = g * kGroupM;
+  const int gm = min(p.tiles_m - first_m, kGroupM);
+  const int r = tile - g * per_group;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+__device__ __forceinline__ float apply_act(float x, int act) {
+  if (act == FA_ACT_RELU) return fmaxf(x, 0.f);
+  if (act == FA_ACT_GELU_TANH) {
+    const float u = 0.7978845608028654f * fmaf(0.044715f * x * x, x, x);
+    const float hx = 0.5f * x;
+    return fmaf(hx, tanh_approx(u), hx);
+  }
+  return x;
+}
+
+__global__ void __launch_bounds__(kGThreads, 1)
+    gemm_act_kernel(const __grid_constant__ CUtensorMap tmA,
+                    const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bars = base + kGBarOff;
+  auto bar_full = [&](int s) { return bars + 8u * s; };
+  auto bar_empty = [&](int s) { return bars + 8u * (kGStages + s); };
+  auto bar_acc_full = [&](int a) { return bars + 8u * (2 * kGStages + a); };
+  auto bar_acc_empty = [&](int a) { return bars + 8u * (2 * kGStages + 2 + a); };
+  const uint32_t bar_drain = bars + 8u * (2 * kGStages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kGMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + kGMiscOff + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nk = p.K / kGBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGStages; ++s) {
+      mbar_init(bar_full(s), 1);
+      mbar_init(bar_empty(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_acc_full(a), 1);
+      mbar_init(bar_acc_empty(a), 128);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // =================== TMA producer ===================
+    if (elect_one()) {
+      const uint64_t pol = l2_policy_evict_last();
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        int tm, tn;
+        tile_coords(p, tile, tm, tn);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kGStages;
+          const uint32_t ph = (it / kGStages) & 1;
+          if (!mbar_wait(bar_empty(s), ph ^ 1u, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + s * kStageBytes;
+          const uint32_t sb = sa + kABytes;
+          mbar_arrive_expect_tx(bar_full(s), kStageBytes);
+          tma_load_2d(sa, &tmA, bar_full(s), kb * kGBK, tm * kGBM, pol);
+#pragma unroll
+          for (int a = 0; a < kGBN / 64; ++a)
+            tma_load_2d(sb + a * 8192, &tmB, bar_full(s), tn * kGBN + a * 64, kb * kGBK, pol);
+        }
+      }
+      if (!ok) {
+        for (int i = max(0, it - kGStages); i < it; ++i)
+          gemm_drain_wait(bar_full(i % kGStages), (i / kGStages) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // =================== MMA issuer ===================
+    if (elect_one()) {
+      constexpr uint32_t kId = idesc_bf16_f32(kGBM, kGBN, false, true);
+      int it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+        const int acc = tcount & 1;
+        const uint32_t use = static_cast<uint32_t>(tcount >> 1);
+        if (!mbar_wait(bar_acc_empty(acc), (use & 1u) ^ 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t dt = tmem + 256u * acc;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kGStages;
+          if (!mbar_wait(bar_full(s), (it / kGStages) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + s * kStageBytes;
+          const uint32_t sb = sa + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kGBK / 16; ++kk) {
+            const uint64_t ad = sdesc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(sb + kk * 2048, 8192, 1024);
+            mma_ss(dt, ad, bd, kId, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar_empty(s));
+        }
+        if (!ok) break;
+        mma_commit(bar_acc_full(acc));
+      }
+      mma_commit(bar_drain);
+      gemm_drain_wait(bar_drain, 0);
+    }
+    __syncwarp();
+  } else {
+    // =================== epilogue (warps 2..5) ===================
+    const int wq = warp & 3;                       // TMEM lane quarter of this warp
+    const int row_in_tile = wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    int tcount = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+      int tm, tn;
+      tile_coords(p, tile, tm, tn);
+      const int acc = tcount & 1;
+      const uint32_t use = static_cast<uint32_t>(tcount >> 1);
+      if (!mbar_wait(bar_acc_full(acc), use & 1u, abort_flag, p.status)) break;
+      tc_fence_after();
+      const int row = tm * kGBM + row_in_tile;
+      __nv_bfloat16* crow = p.c + static_cast<int64_t>(row) * p.ldc + tn * kGBN;
+#pragma unroll 1
+      for (int c = 0; c < kGBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32_wait(tmem + lane_off + 256u * acc + c * 32, r);
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          w[e] = pack_bf16x2(apply_act(__uint_as_float(r[2 * e]), p.act),
+                             apply_act(__uint_as_float(r[2 * e + 1]), p.act));
+        if (row < p.M && tn * kGBN + c * 32 < p.N) {
+          uint4* dst = reinterpret_cast<uint4*>(crow + c * 32);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+          dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar_acc_empty(acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+int g_num_sms[64] = {};
+bool g_gemm_attr[64] = {};
+
+int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int64_t lda,
+                int64_t ldb, int64_t ldc, int act, cudaStream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FA_ERR_CUDA;
+  if (!g_gemm_attr[dev]) {
+    int rc = prepare_device(reinterpret_cast<const void*>(gemm_act_kernel), kGSmemBytes, &dev);
+    if (rc != FA_OK) return rc;
+    cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    g_gemm_attr[dev] = true;
+  }
+  CUtensorMap ma, mb;
+  int rc = make_tmap_2d(&ma, a, M, K, lda, kGBM, 64);
+  if (rc != FA_OK) return rc;
+  rc = make_tmap_2d(&mb, b, K, N, ldb, 64, 64);
+  if (rc != FA_OK) return rc;
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.tiles_m = (M + kGBM - 1) / kGBM;
+  p.tiles_n = (N + kGBN - 1) / kGBN;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.act = act;
+  p.c = static_cast<__nv_bfloat16*>(c);
+  p.ldc = ldc;
+  p.status = device_status_ptr();
+  if (p.status == nullptr) return FA_ERR_CUDA;
+  const int grid = min(p.num_tiles, g_num_sms[dev] > 0 ? g_num_sms[dev] : 148);
+  gemm_act_kernel<<<grid, kGThreads, kGSmemBytes, stream>>>(ma, mb, p);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+int check_gemm_args(const void* a, const void* b, const void* c, int M, int N, int K,
+                    int64_t lda, int64_t ldb, int64_t ldc, int act) {
+  if (!a || !b || !c) return FA_ERR_NULL;
+  if (M <= 0 || N <= 0 || K <= 0) return FA_ERR_SHAPE;
+  if ((K % 64) != 0 || (N % 64) != 0) return FA_ERR_SHAPE;
+  if (act < FA_ACT_NONE || act > FA_ACT_GELU_TANH) return FA_ERR_ARG;
+  if (lda < K || ldb < N || ldc < N) return FA_ERR_STRIDE;
+  if ((lda % 8) || (ldb % 8) || (ldc % 8)) return FA_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+       reinterpret_cast<uintptr_t>(c)) % 16)
+    return FA_ERR_ALIGN;
+  return FA_OK;
+}
+
+}  // namespace
+}  // namespace fa
+
+extern "C" int fa_gemm_act(const void* a, const void* b, void* c, int M, int N, int K,
+                           int64_t lda, int64_t ldb, int64_t ldc, int act, void* stream) {
+  int rc = fa::check_gemm_args(a, b, c, M, N, K, lda, ldb, ldc, act);
+  if (rc != FA_OK) return rc;
+  return fa::launch_gemm(a, b, c, M, N, K, lda, ldb, ldc, act,
+                         static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fa_mlp_fwd(const void* x, const void* w1, const void* w2, void* hidden, void* y,
+                          int M, int K, int N, int act, void* stream) {
+  // hidden[M, N] = act(x[M, K] @ w1[K, N]);  y[M, K] = hidden @ w2[N, K]
+  int rc = fa::check_gemm_args(x, w1, hidden, M, N, K, K, N, N, act);
+  if (rc != FA_OK) return rc;
+  rc = fa::check_gemm_args(hidden, w2, y, M, K, N, N, K, K, FA_ACT_NONE);
+  if (rc != FA_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = fa::launch_gemm(x, w1, hidden, M, N, K, K, N, N, act, s);
+  if (rc != FA_OK) return rc;
+  return fa::launch_gemm(hidden, w2, y, M, K, N, N, K, K, FA_ACT_NONE, s);
+}

@@ -1,0 +1,194 @@
+"""Python operators over the C ABI: the drop-in for the reference's hot path.
+
+* ``attention(q, k, v, causal=False)`` on ``[B, H, S, D]`` bf16 CUDA tensors --
+  the operator behind the reference's kernel-module protocol (``bench.py:14-20``;
+  ``pytorch-naive.py:23-65``, ``flash-attn2-sota.py:41-63``,
+  ``old/kernels/old/naive.py:27-56``).
+* ``attention_bshd(q, k, v, causal=False)`` -- the legacy ``(B, S, H, D)``
+  layout of ``old/benchmark.py:17-21``, passed to the kernel as strides (no
+  permute copy).
+* ``mlp(x, w1, w2)`` -- ``act(x @ w1) @ w2``, the GEMM -> activation -> GEMM of
+  ``run_mlp_search.py:58-69`` with the activation fused into GEMM 1.
+* ``gemm_act(a, b, act)`` -- one matmul stage with its fused epilogue.
+* ``attention_from_host(...)`` -- the same operator fed from (pinned) host
+  tensors: copies in, kernel, copy out, all on the current stream.
+
+Errors: argument problems Python can see (device, dtype, rank) raise
+``TypeError``/``ValueError``; everything the C ABI rejects raises
+``FaError`` (a ``RuntimeError``) carrying ``fa_strerror``'s text, the way the
+reference's modules surface failures as exceptions that ``bench.py:68-74``
+records.  There is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+_BF16 = torch.bfloat16
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check_cuda_bf16(name: str, t: torch.Tensor) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (got device {t.device})")
+    if t.dtype != _BF16:
+        raise TypeError(f"{name} must be bfloat16 (got {t.dtype})")
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+              scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax(q k^T * scale [+ causal mask]) v on ``[B, H, S, D]`` bf16 tensors.
+
+    ``scale`` defaults to ``1/sqrt(D)`` (``run_attention_search.py:40``).
+    Inputs may have arbitrary batch/head/sequence strides (multiples of 8
+    elements) but must be contiguous along D.  Returns a new ``[B, H, S, D]``
+    tensor unless ``out`` is given.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check_cuda_bf16(name, t)
+        if t.dim() != 4:
+            raise ValueError(f"{name} must be 4-D [B, H, S, D] (got {tuple(t.shape)})")
+    if not (q.shape == k.shape == v.shape):
+        raise ValueError(f"q, k, v shapes differ: {tuple(q.shape)}, {tuple(k.shape)}, "
+                         f"{tuple(v.shape)}")
+    if not (q.device == k.device == v.device):
+        raise ValueError("q, k, v must be on the same device")
+    B, H, S, D = q.shape
+    if out is None:
+        out = torch.empty((B, H, S, D), dtype=_BF16, device=q.device)
+    else:
+        _check_cuda_bf16("out", out)
+        if tuple(out.shape) != (B, H, S, D) or out.device != q.device:
+            raise ValueError("out must match q's shape and device")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    lib = _lib.load()
+    strides = (ctypes.c_int64 * 16)(*q.stride(), *k.stride(), *v.stride(), *out.stride())
+    with torch.cuda.device(q.device):
+        rc = lib.fa_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                             B, H, S, D, strides, int(bool(causal)), float(scale),
+                             _stream_ptr(q.device))
+    _lib.check(rc, "fa_attn_fwd")
+    return out
+
+
+def attention_bshd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+                   scale: float | None = None) -> torch.Tensor:
+    """The legacy ``fn(q, k, v)`` on ``(B, S, H, D)`` tensors
+    (``old/benchmark.py:17-21``); the head/sequence transpose is expressed as
+    strides, so no data is copied.  Returns ``(B, S, H, D)``."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check_cuda_bf16(name, t)
+        if t.dim() != 4:
+            raise ValueError(f"{name} must be 4-D (B, S, H, D)")
+    out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    attention(q.permute(0, 2, 1, 3), k.permute(0, 2, 1, 3), v.permute(0, 2, 1, 3),
+              causal=causal, scale=scale, out=out.permute(0, 2, 1, 3))
+    return out
+
+
+def attention_from_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                        causal: bool = False, scale: float | None = None,
+                        out: torch.Tensor | None = None,
+                        device: torch.device | int | str | None = None,
+                        workspace: dict | None = None) -> torch.Tensor:
+    """``attention`` for host tensors: H2D copy of q, k, v, the fused kernel,
+    D2H copy of O, all enqueued on the current stream of ``device``.
+
+    Host tensors should be pinned for the copies to be asynchronous.  The
+    result lands in ``out`` (a host tensor, allocated pinned if omitted); the
+    caller synchronises the stream before reading it.  ``workspace`` (a dict)
+    keeps the device buffers between calls.
+    """
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None \
+        else torch.device(device)
+    if dev.type != "cuda":
+        raise ValueError("device must be a CUDA device")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.is_cuda or t.dtype != _BF16:
+            raise ValueError(f"{name} must be a bfloat16 host tensor")
+    ws = workspace if workspace is not None else {}
+    key = (tuple(q.shape), dev)
+    if ws.get("key") != key:
+        ws.clear()
+        ws["key"] = key
+        for name in ("q", "k", "v", "o"):
+            ws[name] = torch.empty(q.shape, dtype=_BF16, device=dev)
+    ws["q"].copy_(q, non_blocking=True)
+    ws["k"].copy_(k, non_blocking=True)
+    ws["v"].copy_(v, non_blocking=True)
+    attention(ws["q"], ws["k"], ws["v"], causal=causal, scale=scale, out=ws["o"])
+    if out is None:
+        out = torch.empty(q.shape, dtype=_BF16, pin_memory=True)
+    out.copy_(ws["o"], non_blocking=True)
+    return out
+
+
+def gemm_act(a: torch.Tensor, b: torch.Tensor, act: str = "none",
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """``act(a @ b)`` for row-major bf16 ``a [M, K]``, ``b [K, N]``; K and N
+    multiples of 64."""
+    _check_cuda_bf16("a", a)
+    _check_cuda_bf16("b", b)
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError(f"bad GEMM shapes {tuple(a.shape)} @ {tuple(b.shape)}")
+    if a.stride(1) != 1 or b.stride(1) != 1:
+        raise ValueError("a and b must be row-major (last dimension contiguous)")
+    if act not in _lib.ACTIVATIONS:
+        raise ValueError(f"act must be one of {sorted(_lib.ACTIVATIONS)}")
+    M, K = a.shape
+    N = b.shape[1]
+    if out is None:
+        out = torch.empty((M, N), dtype=_BF16, device=a.device)
+    lib = _lib.load()
+    with torch.cuda.device(a.device):
+        rc = lib.fa_gemm_act(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
+                             a.stride(0), b.stride(0), out.stride(0),
+                             _lib.ACTIVATIONS[act], _stream_ptr(a.device))
+    _lib.check(rc, "fa_gemm_act")
+    return out
+
+
+def mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, act: str = "gelu_tanh",
+        hidden: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``act(x @ w1) @ w2`` with ``x [M, K]``, ``w1 [K, N]``, ``w2 [N, K]``
+    (row-major bf16, K and N multiples of 64).  ``act`` is "gelu_tanh" (the
+    benchmark block) or "relu" (``run_mlp_search.py:62-64``).  ``hidden`` is
+    the ``[M, N]`` bf16 workspace for ``act(x @ w1)``."""
+    for name, t in (("x", x), ("w1", w1), ("w2", w2)):
+        _check_cuda_bf16(name, t)
+        if t.dim() != 2 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous 2-D tensor")
+    M, K = x.shape
+    if w1.shape[0] != K or w2.shape[1] != K or w2.shape[0] != w1.shape[1]:
+        raise ValueError(f"bad MLP shapes x{tuple(x.shape)} w1{tuple(w1.shape)} "
+                         f"w2{tuple(w2.shape)}")
+    N = w1.shape[1]
+    if act not in ("gelu_tanh", "relu"):
+        raise ValueError("act must be 'gelu_tanh' or 'relu'")
+    if hidden is None:
+        hidden = torch.empty((M, N), dtype=_BF16, device=x.device)
+    if out is None:
+        out = torch.empty((M, K), dtype=_BF16, device=x.device)
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.fa_mlp_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), hidden.data_ptr(),
+                            out.data_ptr(), M, K, N, _lib.ACTIVATIONS[act],
+                            _stream_ptr(x.device))
+    _lib.check(rc, "fa_mlp_fwd")
+    return out
+
+
+def device_status() -> int:
+    """Read and clear the device-side status word (FA_OK or FA_ERR_TIMEOUT)."""
+    return _lib.load().fa_device_status()

@@ -1,0 +1,109 @@
+/*
+ * fa_b200.h -- C ABI of the B200 (sm_100a) attention / MLP hot path.
+ *
+ * Library: libfa_b200.so (built by cs348k_fast_attention_grammar_b200/build.py).
+ * All entry points are stream-ordered and asynchronous on the caller's
+ * stream; none of them allocates device memory, and the caller owns every
+ * buffer.  Every function returns an fa_status (0 = success); no C++
+ * exception crosses this boundary.  Tensors are bf16 (raw 16-bit words),
+ * pointers are device pointers, strides are in elements.
+ *
+ * Reference interfaces replaced (paths inside nriedman/cs348k-fast-attention-grammar):
+ *   fa_attn_fwd  <- the attention operator behind the kernel-module protocol
+ *                   that bench.py:14-20 times: the host callable fn(KT, Q, V)
+ *                   emitted at grammar/kernel_ast.py:1267-1287 (e.g.
+ *                   runs/attn_full/kernels/best_it24.py:78-99), the torch
+ *                   modules pytorch-naive.py:23-65 and flash-attn2-sota.py:41-63,
+ *                   and the batched attention(q, k, v) of
+ *                   old/kernels/old/naive.py:27-56 / old/benchmark.py:17-21.
+ *   fa_mlp_fwd   <- the host callable emitted for the MLP program of
+ *                   run_mlp_search.py:42-127 (stages h = X@W1, a = act(h),
+ *                   y = a@W2 at :58-69).
+ *   fa_gemm_act  <- one matmul stage with its pointwise epilogue, the
+ *                   "matmul" reduction rule grammar/kernel_ast.py:207-211
+ *                   (ct.mma K-loop) followed by the relu stage of
+ *                   run_mlp_search.py:62-64.
+ */
+#ifndef FA_B200_H_
+#define FA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum fa_status {
+  FA_OK = 0,
+  FA_ERR_NULL = 1,         /* a required pointer is NULL                        */
+  FA_ERR_SHAPE = 2,        /* a dimension is <= 0 or too large                  */
+  FA_ERR_HEAD_DIM = 3,     /* head dim not supported (attention: 64 or 128)     */
+  FA_ERR_ALIGN = 4,        /* pointer or stride not 16-byte aligned (TMA rule)  */
+  FA_ERR_STRIDE = 5,       /* innermost stride is not 1                         */
+  FA_ERR_TMA = 6,          /* cuTensorMapEncodeTiled rejected the tensor        */
+  FA_ERR_LAUNCH = 7,       /* kernel launch failed (cudaGetLastError)           */
+  FA_ERR_DRIVER = 8,       /* driver entry point unavailable                    */
+  FA_ERR_DEVICE = 9,       /* current device is not sm_100 (B200 class)         */
+  FA_ERR_ARG = 10,         /* an enum argument is out of range                  */
+  FA_ERR_TIMEOUT = 11,     /* a kernel wait ran out (read by fa_device_status)  */
+  FA_ERR_CUDA = 12         /* another CUDA runtime call failed                  */
+} fa_status;
+
+typedef enum fa_activation {
+  FA_ACT_NONE = 0,
+  FA_ACT_RELU = 1,         /* run_mlp_search.py:62-64                           */
+  FA_ACT_GELU_TANH = 2     /* 0.5x(1+tanh(sqrt(2/pi)(x+0.044715x^3)))           */
+} fa_activation;
+
+/* Human-readable text for a status code (static storage). */
+const char* fa_strerror(int status);
+
+/* Library version as major*10000 + minor*100 + patch. */
+int fa_version(void);
+
+/*
+ * Fused attention forward  O = softmax(Q K^T * scale [+ causal mask]) V.
+ *   q, k, v, o : [B, H, S, D] bf16, element strides
+ *                strides[0..3] = q (b, h, s, d), strides[4..7] = k,
+ *                strides[8..11] = v, strides[12..15] = o; every d-stride must
+ *                be 1 and every other stride a multiple of 8 elements.
+ *   D          : 64 or 128.
+ *   causal     : nonzero = key j visible to query i iff j <= i.
+ *   scale      : softmax scale (pass 1/sqrt(D) for the reference's math).
+ *   stream     : cudaStream_t (NULL = legacy default stream).
+ * Computes in fp32 (tcgen05 bf16 MMAs with fp32 accumulation in TMEM).
+ */
+int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S,
+                int D, const int64_t* strides, int causal, float scale, void* stream);
+
+/*
+ * C[M, N] = act(A[M, K] @ B[K, N]) in bf16 with fp32 accumulation.
+ *   A row-major with row stride lda (K contiguous); B row-major [K, N] with
+ *   row stride ldb (N contiguous); C row-major with row stride ldc.
+ *   K and N must be multiples of 64, M any positive value; lda, ldb, ldc
+ *   multiples of 8.
+ */
+int fa_gemm_act(const void* a, const void* b, void* c, int M, int N, int K, int64_t lda,
+                int64_t ldb, int64_t ldc, int act, void* stream);
+
+/*
+ * MLP block Y[M, K] = act(X[M, K] @ W1[K, N]) @ W2[N, K]   (all row-major bf16).
+ *   hidden : caller-owned [M, N] bf16 workspace that receives act(X @ W1).
+ *   K, N multiples of 64.  act = FA_ACT_GELU_TANH for the benchmark block,
+ *   FA_ACT_RELU for the reference's.
+ */
+int fa_mlp_fwd(const void* x, const void* w1, const void* w2, void* hidden, void* y, int M,
+               int K, int N, int act, void* stream);
+
+/*
+ * Reads and clears the device-side status word of the current device
+ * (FA_OK, or FA_ERR_TIMEOUT when a kernel's bounded wait ran out).
+ * Synchronises the device.
+ */
+int fa_device_status(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_B200_H_ */

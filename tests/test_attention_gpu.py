@@ -1,0 +1,179 @@
+"""Parity of the sm_100a attention kernel (through the C ABI) with the CPU
+oracle and with the reference's own outputs (golden vectors).
+
+Tolerance: max abs error <= 2e-2 and mean abs error
+<= 2e-3 against the fp32 oracle, for bf16 inputs with fp32 accumulation.
+"""
+
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, assert_close
+import oracle
+from cs348k_fast_attention_grammar_b200 import (FaError, attention, attention_bshd,
+                                                attention_from_host, device_status)
+from cs348k_fast_attention_grammar_b200 import kernel_module
+from cs348k_fast_attention_grammar_b200.inputs import ATTN_CONFIGS, make_qkv
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _rand(shape, seed, amp=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * amp).to(torch.bfloat16)
+
+
+def _run(q, k, v, causal):
+    out = torch.full(q.shape, float("nan"), dtype=torch.bfloat16, device=DEV)
+    attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal, out=out)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("B,H,S", [(1, 2, 128), (2, 3, 256), (1, 2, 384), (1, 1, 200),
+                                   (1, 2, 1000), (1, 1, 1), (1, 1, 130), (2, 1, 512)])
+def test_attention_matches_oracle(B, H, S, D, causal):
+    q, k, v = (_rand((B, H, S, D), 10 + i) for i in range(3))
+    out = _run(q, k, v, causal)
+    ref = oracle.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                           causal=causal)
+    assert_close(out, ref, what=f"B{B} H{H} S{S} D{D} causal={causal}")
+
+
+@pytest.mark.parametrize("name", ["attn_program_N512_d64", "attn_program_N256_d128",
+                                  "attn_program_N128_d64", "attn_best_it24_N512_d64"])
+def test_attention_matches_reference_program(name):
+    """Golden vectors from the reference's emitted cuTile programs (run through
+    its numpy stand-in); inputs are bf16 values, layout KT [d, N]."""
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    out = kernel_module.fn(torch.from_numpy(z["KT"]).to(DEV), torch.from_numpy(z["Q"]).to(DEV),
+                           torch.from_numpy(z["V"]).to(DEV))
+    torch.cuda.synchronize()
+    assert_close(out.cpu().numpy(), z["O"], what=name)
+
+
+def test_attention_matches_sota_module():
+    z = np.load(os.path.join(GOLDEN, "sdpa_N512_d64.npz"))
+    out = kernel_module.sota_fn(*(torch.from_numpy(z[n]).to(DEV) for n in ("K", "Q", "V")))
+    assert_close(out.cpu().numpy(), z["O"], what="sdpa_N512_d64")
+
+
+@pytest.mark.parametrize("name", ["sdpa_causal_S384_d128", "sdpa_causal_S200_d64"])
+def test_attention_causal_matches_sdpa_golden(name):
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    q, k, v = (torch.from_numpy(z[n]).to(torch.bfloat16) for n in ("Q", "K", "V"))
+    out = _run(q, k, v, causal=True)
+    assert_close(out, z["O"], what=name)
+
+
+def test_bshd_layout_is_bit_identical():
+    B, S, H, D = 2, 384, 3, 128
+    q, k, v = (_rand((B, S, H, D), 20 + i).to(DEV) for i in range(3))
+    o1 = attention_bshd(q, k, v, causal=True)
+    o2 = attention(q.permute(0, 2, 1, 3).contiguous(), k.permute(0, 2, 1, 3).contiguous(),
+                   v.permute(0, 2, 1, 3).contiguous(), causal=True)
+    torch.cuda.synchronize()
+    assert torch.equal(o1.permute(0, 2, 1, 3), o2)
+
+
+def test_from_host_matches_device_call():
+    q, k, v = (_rand((1, 2, 256, 64), 30 + i).pin_memory() for i in range(3))
+    o_host = attention_from_host(q, k, v, causal=False, device=DEV)
+    torch.cuda.synchronize()
+    o_dev = attention(q.to(DEV), k.to(DEV), v.to(DEV))
+    assert torch.equal(o_host, o_dev.cpu())
+
+
+def test_repeated_calls_are_deterministic():
+    q, k, v = (_rand((2, 4, 1024, 128), 40 + i).to(DEV) for i in range(3))
+    a = attention(q, k, v, causal=True)
+    b = attention(q, k, v, causal=True)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert device_status() == 0
+
+
+def test_error_codes():
+    q = _rand((1, 1, 128, 96), 1).to(DEV)
+    with pytest.raises(FaError, match="head dimension"):
+        attention(q, q, q)
+    ok = _rand((1, 1, 128, 64), 2).to(DEV)
+    flat = torch.zeros(128 * 65 + 64, dtype=torch.bfloat16, device=DEV)
+    odd = flat.as_strided((1, 1, 128, 64), (128 * 65, 128 * 65, 65, 1))   # row stride 130 B
+    with pytest.raises(FaError, match="aligned"):
+        attention(odd, ok, ok)
+    with pytest.raises(FaError, match="innermost stride"):
+        attention(ok.transpose(2, 3).contiguous().transpose(2, 3), ok, ok)
+    with pytest.raises(ValueError):
+        attention(q.cpu(), q.cpu(), q.cpu())
+    with pytest.raises(TypeError):
+        attention(q.float(), q.float(), q.float())
+
+
+# ---------------------------------------------------------------------------
+# Full BASELINE sizes: a seeded subset of pairs against a torch fp32
+# reference on the GPU, plus size-independent properties.
+# ---------------------------------------------------------------------------
+def _torch_ref_pair(q, k, v, causal, row_chunk=2048):
+    qf, kf, vf = q.float(), k.float(), v.float()
+    S, D = qf.shape
+    out = torch.empty_like(qf)
+    for r0 in range(0, S, row_chunk):
+        s = (qf[r0:r0 + row_chunk] @ kf.t()) / math.sqrt(D)
+        if causal:
+            rows = torch.arange(r0, min(S, r0 + row_chunk), device=q.device)[:, None]
+            s = s.masked_fill(torch.arange(S, device=q.device)[None, :] > rows, float("-inf"))
+        out[r0:r0 + row_chunk] = torch.softmax(s, dim=-1) @ vf
+    return out
+
+
+@pytest.mark.parametrize("cfg_name", ["cfg1", "cfg2"])
+def test_full_size_subset(cfg_name):
+    cfg = ATTN_CONFIGS[cfg_name]
+    npairs = cfg["B"] * cfg["H"]
+    q, k, v = make_qkv(cfg, range(npairs), DEV)
+    q = q.view(cfg["B"], cfg["H"], cfg["S"], cfg["D"])
+    k = k.view_as(q)
+    v = v.view_as(q)
+    o = attention(q, k, v, causal=cfg["causal"])
+    rng = np.random.default_rng(123)
+    for p in rng.choice(npairs, size=4, replace=False):
+        b, h = divmod(int(p), cfg["H"])
+        ref = _torch_ref_pair(q[b, h], k[b, h], v[b, h], cfg["causal"])
+        d = (o[b, h].float() - ref).abs()
+        assert d.max().item() <= 2e-2 and d.mean().item() <= 2e-3, (cfg_name, p, d.max().item())
+    assert torch.isfinite(o.float()).all()
+
+
+def test_property_constant_v_gives_constant_output():
+    """Rows of P sum to one: V = c everywhere gives O = c (all S, causal)."""
+    B, H, S, D = 1, 2, 3000, 128
+    q, k = _rand((B, H, S, D), 50).to(DEV), _rand((B, H, S, D), 51).to(DEV)
+    v = torch.full((B, H, S, D), 0.75, dtype=torch.bfloat16, device=DEV)
+    for causal in (False, True):
+        o = attention(q, k, v, causal=causal).float()
+        assert (o - 0.75).abs().max().item() < 4e-3
+
+
+def test_property_causal_first_row_is_v0():
+    B, H, S, D = 1, 2, 2048, 64
+    q, k, v = (_rand((B, H, S, D), 60 + i).to(DEV) for i in range(3))
+    o = attention(q, k, v, causal=True)
+    assert (o[:, :, 0].float() - v[:, :, 0].float()).abs().max().item() < 1e-2
+
+
+def test_property_key_permutation_invariance():
+    """Non-causal attention is invariant under a joint permutation of K/V rows."""
+    B, H, S, D = 1, 2, 1024, 128
+    q, k, v = (_rand((B, H, S, D), 70 + i).to(DEV) for i in range(3))
+    perm = torch.randperm(S, generator=torch.Generator().manual_seed(0)).to(DEV)
+    o1 = attention(q, k, v).float()
+    o2 = attention(q, k[:, :, perm].contiguous(), v[:, :, perm].contiguous()).float()
+    assert (o1 - o2).abs().max().item() < 2e-2

@@ -1,0 +1,95 @@
+"""Parity of the sm_100a GEMM (+fused activation) and MLP block with the
+oracle and the reference's golden MLP vectors.
+
+Tolerance: max abs <= 2e-2, mean abs <= 2e-3 against the fp32 oracle on the
+same bf16 inputs.  The hidden activation is stored in bf16 by design, so the
+second GEMM is compared with an oracle that rounds the hidden tensor to bf16
+too (``round_hidden_bf16``); the unrounded oracle is checked with a looser
+bound that covers that storage rounding.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, assert_close
+import oracle
+from oracle.mlp import round_to_bf16
+from cs348k_fast_attention_grammar_b200 import FaError, gemm_act, mlp
+from cs348k_fast_attention_grammar_b200.inputs import MLP_CONFIGS, make_mlp
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _rand(shape, seed, std=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * std).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("act", ["none", "relu", "gelu_tanh"])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 256), (200, 320, 192),
+                                   (1, 64, 64), (1000, 768, 512)])
+def test_gemm_act_matches_oracle(M, N, K, act):
+    a = _rand((M, K), 1)
+    b = _rand((K, N), 2, std=K ** -0.5)
+    out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=DEV)
+    gemm_act(a.to(DEV), b.to(DEV), act=act, out=out)
+    torch.cuda.synchronize()
+    h = a.double().numpy() @ b.double().numpy()
+    ref = {"none": h, "relu": np.maximum(h, 0), "gelu_tanh": oracle.gelu_tanh(h)}[act]
+    assert_close(out.float().cpu().numpy(), ref, what=f"gemm {M}x{N}x{K} {act}")
+
+
+@pytest.mark.parametrize("act", ["relu", "gelu_tanh"])
+def test_mlp_matches_oracle(act):
+    M, K, N = 384, 256, 1024
+    x = _rand((M, K), 3)
+    w1 = _rand((K, N), 4, std=K ** -0.5)
+    w2 = _rand((N, K), 5, std=N ** -0.5)
+    y = mlp(x.to(DEV), w1.to(DEV), w2.to(DEV), act=act)
+    torch.cuda.synchronize()
+    xs, w1s, w2s = (t.float().numpy() for t in (x, w1, w2))
+    ref = oracle.mlp(xs, w1s, w2s, act=act, round_hidden_bf16=True)
+    assert_close(y.float().cpu().numpy(), ref, what=f"mlp {act}")
+    ref_exact = oracle.mlp(xs, w1s, w2s, act=act)
+    assert_close(y.float().cpu().numpy(), ref_exact, max_tol=5e-2, mean_tol=5e-3,
+                 what=f"mlp {act} vs unrounded hidden")
+
+
+def test_mlp_matches_reference_relu_core_golden():
+    """The reference's GEMM -> ReLU -> GEMM program (grammar nodes as
+    run_mlp_search.py:58-69 writes them), run by its numpy stand-in."""
+    z = np.load(os.path.join(GOLDEN, "mlp_relu_core_B64_Dm64_H128.npz"))
+    x, w1, w2 = (torch.from_numpy(z[n]).to(torch.bfloat16).to(DEV) for n in ("X", "W1", "W2"))
+    y = mlp(x, w1, w2, act="relu")
+    hidden_ref = round_to_bf16(np.maximum(z["X"].astype(np.float64) @ z["W1"], 0))
+    ref = hidden_ref.astype(np.float64) @ z["W2"]
+    assert_close(y.float().cpu().numpy(), ref, what="relu core vs bf16-hidden oracle")
+    assert_close(y.float().cpu().numpy(), z["O"], max_tol=5e-2, mean_tol=5e-3,
+                 what="relu core vs reference program")
+
+
+def test_mlp_full_size_rows():
+    """BASELINE MLP config at full size; a seeded subset of rows against a
+    torch fp32 reference on the GPU."""
+    cfg = MLP_CONFIGS["cfg3"]
+    x, w1, w2 = make_mlp(cfg, DEV)
+    y = mlp(x, w1, w2, act="gelu_tanh")
+    rows = torch.from_numpy(np.random.default_rng(0).choice(cfg["M"], 64, replace=False)).to(DEV)
+    h = torch.nn.functional.gelu(x[rows].float() @ w1.float(), approximate="tanh")
+    ref = h.to(torch.bfloat16).float() @ w2.float()
+    d = (y[rows].float() - ref).abs()
+    assert d.max().item() <= 2e-2 and d.mean().item() <= 2e-3, d.max().item()
+    assert torch.isfinite(y.float()).all()
+
+
+def test_gemm_errors():
+    a = _rand((128, 96), 1).to(DEV)
+    b = _rand((96, 128), 2).to(DEV)
+    with pytest.raises(FaError, match="shape"):
+        gemm_act(a, b)
+    with pytest.raises(ValueError):
+        gemm_act(a, b, act="tanh")
