@@ -118,6 +118,8 @@ extern "C" const char* fa_strerror(int status) {
     case FA_ERR_ARG: return "argument out of range";
     case FA_ERR_TIMEOUT: return "a kernel wait exceeded its time limit (device status)";
     case FA_ERR_CUDA: return "a CUDA runtime call failed";
+    case FA_ERR_SCRATCH:
+      return "M * N exceeds the fixed hidden buffer of fa_mlp_fwd_noalloc (8,388,608 elements)";
     default: return "unknown fa_status";
   }
 }

@@ -16,6 +16,8 @@
 //               epilogue of tile i overlap the main loop of tile i+1.
 #include <cuda_bf16.h>
 
+#include <mutex>
+
 #include "fa_internal.h"
 #include "sm100_ptx.cuh"
 #include "sm100_tmem_wide.cuh"
@@ -282,6 +284,60 @@ int check_gemm_args(const void* a, const void* b, const void* c, int M, int N, i
 
 }  // namespace
 }  // namespace fa
+
+// ---------------------------------------------------------------------------
+// MLP block whose hidden buffer is a fixed array inside this library, for
+// callers that cannot allocate device memory.  Every GPU that loads the
+// library holds this array (16 MiB) until the process exits.
+// ---------------------------------------------------------------------------
+namespace fa {
+namespace {
+
+constexpr int64_t kNoAllocHiddenElems = 8ll * 1024 * 1024;   // 16 MiB of bf16
+
+// The hidden activation act(X @ W1) of fa_mlp_fwd_noalloc.  From host code
+// this name is only a handle: its device address comes from
+// cudaGetSymbolAddress on the device that runs the kernels.
+static __device__ __align__(256) __nv_bfloat16 g_mlp_hidden_scratch[kNoAllocHiddenElems];
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[64] = {};
+
+// Device address of g_mlp_hidden_scratch on the current device, looked up
+// once per device (the first call on a device does the lookup).
+int hidden_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FA_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_mlp_hidden_scratch) != cudaSuccess || p == nullptr)
+      return FA_ERR_CUDA;
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return FA_OK;
+}
+
+}  // namespace
+}  // namespace fa
+
+extern "C" int fa_mlp_fwd_noalloc(const void* x, const void* w1, const void* w2, void* y, int M,
+                                  int K, int N, int act, void* stream) {
+  if (M > 0 && N > 0 && static_cast<int64_t>(M) * N > fa::kNoAllocHiddenElems)
+    return FA_ERR_SCRATCH;
+  void* hidden = nullptr;
+  int rc = fa::hidden_scratch_address(&hidden);
+  if (rc != FA_OK) return rc;
+  rc = fa::check_gemm_args(x, w1, hidden, M, N, K, K, N, N, act);
+  if (rc != FA_OK) return rc;
+  rc = fa::check_gemm_args(hidden, w2, y, M, K, N, N, K, K, FA_ACT_NONE);
+  if (rc != FA_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = fa::launch_gemm(x, w1, hidden, M, N, K, K, N, N, act, s);
+  if (rc != FA_OK) return rc;
+  return fa::launch_gemm(hidden, w2, y, M, K, N, N, K, K, FA_ACT_NONE, s);
+}
 
 extern "C" int fa_gemm_act(const void* a, const void* b, void* c, int M, int N, int K,
                            int64_t lda, int64_t ldb, int64_t ldc, int act, void* stream) {

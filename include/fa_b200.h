@@ -46,7 +46,8 @@ typedef enum fa_status {
   FA_ERR_DEVICE = 9,       /* current device is not sm_100 (B200 class)         */
   FA_ERR_ARG = 10,         /* an enum argument is out of range                  */
   FA_ERR_TIMEOUT = 11,     /* a kernel wait ran out (read by fa_device_status)  */
-  FA_ERR_CUDA = 12         /* another CUDA runtime call failed                  */
+  FA_ERR_CUDA = 12,        /* another CUDA runtime call failed                  */
+  FA_ERR_SCRATCH = 13      /* problem exceeds fa_mlp_fwd_noalloc's fixed buffer */
 } fa_status;
 
 typedef enum fa_activation {
@@ -94,6 +95,28 @@ int fa_gemm_act(const void* a, const void* b, void* c, int M, int N, int K, int6
  */
 int fa_mlp_fwd(const void* x, const void* w1, const void* w2, void* hidden, void* y, int M,
                int K, int N, int act, void* stream);
+
+/*
+ * fa_mlp_fwd without any device allocation: the same MLP block, with the
+ * hidden activation kept in a fixed array inside the library instead of a
+ * caller-provided buffer.  No counterpart in the reference.
+ *   For callers that cannot call cudaMalloc or any allocator -- a plugin
+ *   running inside a host whose memory pools it does not own, code that
+ *   must not allocate while a CUDA graph is being built or while another
+ *   component holds the device's memory budget.  They still pass X, W1, W2
+ *   and Y.
+ *   Limit: M * N <= 8,388,608 hidden elements (a 16 MiB bf16 array that every
+ *   GPU loading the library keeps until the process exits); larger problems
+ *   return FA_ERR_SCRATCH.  Other shape rules as fa_mlp_fwd.
+ *   The first call on each device looks up the array's device address
+ *   (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   All calls share the one array and it keeps the last call's contents
+ *   (every element a call reads it first writes), so calls that may run at
+ *   the same time on the GPU -- on different streams, or from different
+ *   threads -- race and must be serialised by the caller.
+ */
+int fa_mlp_fwd_noalloc(const void* x, const void* w1, const void* w2, void* y, int M, int K,
+                       int N, int act, void* stream);
 
 /*
  * Reads and clears the device-side status word of the current device

@@ -1,0 +1,74 @@
+"""fa_mlp_fwd_noalloc: the MLP block for callers that cannot allocate device
+memory (a plugin inside a host that owns every memory pool, code that must not
+allocate while a graph is built or while another component holds the memory
+budget).  It keeps the hidden activation in a fixed 16 MiB array inside the
+library instead of a caller buffer.
+
+Called through the C ABI and compared with the allocating entry point
+fa_mlp_fwd (caller-provided hidden buffer) on two calls in a row with
+different inputs, so a stale hidden array from the previous call would show.
+This file is named to be collected last.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+from conftest import assert_close
+from cs348k_fast_attention_grammar_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+FA_ERR_SCRATCH = 13
+MAX_HIDDEN_ELEMS = 8 * 1024 * 1024
+
+
+def _noalloc_fn():
+    lib = _lib.load()
+    fn = lib.fa_mlp_fwd_noalloc
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    return lib, fn
+
+
+def _inputs(M, K, N, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(DEV)
+    w1 = (torch.randn(K, N, generator=g) / K ** 0.5).to(torch.bfloat16).to(DEV)
+    w2 = (torch.randn(N, K, generator=g) / N ** 0.5).to(torch.bfloat16).to(DEV)
+    return x, w1, w2
+
+
+def test_noalloc_matches_allocating_mlp_twice():
+    lib, fn = _noalloc_fn()
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+    calls = [(512, 256, 2048, "gelu_tanh", 11), (384, 192, 4096, "relu", 12)]
+    for M, K, N, act, seed in calls:
+        x, w1, w2 = _inputs(M, K, N, seed)
+        a = _lib.ACTIVATIONS[act]
+        hidden = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+        y_ref = torch.empty(M, K, dtype=torch.bfloat16, device=DEV)
+        rc = lib.fa_mlp_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), hidden.data_ptr(),
+                            y_ref.data_ptr(), M, K, N, a, stream)
+        assert rc == 0, _lib.strerror(rc)
+        y = torch.full((M, K), float("nan"), dtype=torch.bfloat16, device=DEV)
+        rc = fn(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), y.data_ptr(), M, K, N, a, stream)
+        assert rc == 0, _lib.strerror(rc)
+        torch.cuda.synchronize()
+        assert_close(y.float().cpu().numpy(), y_ref.float().cpu().numpy(),
+                     what=f"noalloc vs fa_mlp_fwd M{M} K{K} N{N} {act}")
+
+
+def test_noalloc_rejects_hidden_larger_than_its_array():
+    lib, fn = _noalloc_fn()
+    M, K, N = 4096, 64, 4096            # M * N = 16,777,216 > 8,388,608
+    assert M * N > MAX_HIDDEN_ELEMS
+    x = torch.empty(M, K, dtype=torch.bfloat16, device=DEV)
+    w1 = torch.empty(K, N, dtype=torch.bfloat16, device=DEV)
+    w2 = torch.empty(N, K, dtype=torch.bfloat16, device=DEV)
+    y = torch.empty(M, K, dtype=torch.bfloat16, device=DEV)
+    rc = fn(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), y.data_ptr(), M, K, N,
+            _lib.FA_ACT_GELU_TANH, torch.cuda.current_stream(DEV).cuda_stream)
+    assert rc == FA_ERR_SCRATCH
+    assert "fixed hidden buffer" in _lib.strerror(rc)
