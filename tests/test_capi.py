@@ -1,0 +1,91 @@
+"""The C-ABI library: it loads on a machine without a GPU, exports every
+symbol include/fa_b200.h declares, and its host-side argument checks return
+the documented status codes before any device work.  No compute calls."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from cs348k_fast_attention_grammar_b200 import _lib
+
+HEADER = os.path.join(ROOT, "include", "fa_b200.h")
+
+
+def _declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(fa_[a-z0-9_]+)\s*\(", text)))
+
+
+def _declared_status_codes():
+    text = open(HEADER).read()
+    return {m[0]: int(m[1]) for m in re.findall(r"\b(FA_(?:OK|ERR_[A-Z_]+))\s*=\s*(\d+)", text)}
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = _declared_functions()
+    assert {"fa_attn_fwd", "fa_mlp_fwd", "fa_gemm_act", "fa_strerror"} <= set(names)
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in fa_b200.h but not exported"
+
+
+def test_python_binding_covers_header():
+    bound = set(_lib.SIGNATURES)
+    declared = set(_declared_functions())
+    # every bound name is declared; the no-alloc variant is bound where used
+    assert bound <= declared
+    assert declared - bound <= {"fa_mlp_fwd_noalloc"}
+
+
+def test_strerror_for_every_status_code():
+    codes = _declared_status_codes()
+    assert codes["FA_OK"] == 0 and len(codes) >= 13
+    texts = {c: _lib.strerror(v) for c, v in codes.items()}
+    assert texts["FA_OK"] == "success"
+    assert len(set(texts.values())) == len(texts)          # all distinct
+    assert _lib.strerror(999) == "unknown fa_status"
+
+
+def test_version():
+    assert _lib.load().fa_version() >= 100
+
+
+def test_argument_checks_without_device():
+    """Checks that run before any CUDA call return their codes on a CPU box."""
+    lib = _lib.load()
+    st = (ctypes.c_int64 * 16)(*([8192, 1024, 64, 1] * 4))
+    p = ctypes.c_void_p(256)
+    codes = _declared_status_codes()
+    assert lib.fa_attn_fwd(None, p, p, p, 1, 1, 16, 64, st, 0, 0.125, None) == codes["FA_ERR_NULL"]
+    assert lib.fa_attn_fwd(p, p, p, p, 0, 1, 16, 64, st, 0, 0.125, None) == codes["FA_ERR_SHAPE"]
+    assert lib.fa_attn_fwd(p, p, p, p, 1, 1, 16, 96, st, 0, 0.125, None) == \
+        codes["FA_ERR_HEAD_DIM"]
+    bad = (ctypes.c_int64 * 16)(*([8192, 1024, 65, 1] * 4))
+    assert lib.fa_attn_fwd(p, p, p, p, 1, 1, 16, 64, bad, 0, 0.125, None) == codes["FA_ERR_ALIGN"]
+    bad = (ctypes.c_int64 * 16)(*([8192, 1024, 64, 2] * 4))
+    assert lib.fa_attn_fwd(p, p, p, p, 1, 1, 16, 64, bad, 0, 0.125, None) == \
+        codes["FA_ERR_STRIDE"]
+    odd = ctypes.c_void_p(258)
+    assert lib.fa_attn_fwd(odd, p, p, p, 1, 1, 16, 64, st, 0, 0.125, None) == \
+        codes["FA_ERR_ALIGN"]
+    assert lib.fa_gemm_act(p, p, p, 128, 100, 64, 64, 100, 100, 0, None) == codes["FA_ERR_SHAPE"]
+    assert lib.fa_gemm_act(p, p, p, 128, 128, 64, 64, 128, 128, 7, None) == codes["FA_ERR_ARG"]
+    assert lib.fa_gemm_act(p, p, p, 128, 128, 64, 60, 128, 128, 0, None) == \
+        codes["FA_ERR_STRIDE"]
+    fn = lib.fa_mlp_fwd_noalloc
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    assert fn(p, p, p, p, 4096, 64, 4096, 2, None) == codes["FA_ERR_SCRATCH"]
+
+
+def test_no_cpu_fallback_in_package():
+    """The product package never imports the oracle."""
+    pkg = os.path.join(ROOT, "cs348k_fast_attention_grammar_b200")
+    for fn in os.listdir(pkg):
+        if fn.endswith(".py"):
+            src = open(os.path.join(pkg, fn)).read()
+            assert "import oracle" not in src and "from oracle" not in src, fn
