@@ -41,6 +41,65 @@ constexpr int kBN = 128;          // keys per KV block
 constexpr int kThreads = 384;
 constexpr float kRescaleThreshold = 8.0f;
 
+// Share of the softmax exponentials computed on the FMA pipe instead of MUFU:
+// pair c of a row (of 64) is emulated when c % mod == mod - 1 (0 = none).
+#ifndef FA_ATTN_EMU_MOD_D64
+#define FA_ATTN_EMU_MOD_D64 4
+#endif
+#ifndef FA_ATTN_EMU_MOD_D128
+#define FA_ATTN_EMU_MOD_D128 0
+#endif
+// 1 = pack probabilities to bf16 with integer ops (round half up), 0 = cvt.
+#ifndef FA_ATTN_PACK_ALU
+#define FA_ATTN_PACK_ALU 0
+#endif
+// 1 = the two softmax warpgroups take turns on their exp phases.
+#ifndef FA_ATTN_PINGPONG
+#define FA_ATTN_PINGPONG 1
+#endif
+// 1 = move registers from the producer/MMA warpgroup (56 per thread) to the
+// two softmax warpgroups (224 per thread) with setmaxnreg.  The split adds up
+// to the launch's 384 threads x 168 registers exactly.
+#ifndef FA_ATTN_SETMAXNREG
+#define FA_ATTN_SETMAXNREG 1
+#endif
+
+// Degree-3 minimax (relative error) polynomial for 2^f on [-1/2, 1/2],
+// max relative error 7.5e-5; fitted by fit_exp2_poly.py (Remez exchange).
+constexpr float kExpC0 = 0.9999280571937561f;
+constexpr float kExpC1 = 0.6932609677314758f;
+constexpr float kExpC2 = 0.2426111251115799f;
+constexpr float kExpC3 = 0.0551716685295105f;
+
+// 2^x on the FMA/ALU pipes: x = j + f with j = round(x) (the 1.5 * 2^23
+// addition leaves j in the low mantissa bits of t), 2^x = p(f) * 2^j with 2^j
+// applied by adding j to the exponent field.  x is clamped to -125 so the
+// result stays a normal number (2^-125 instead of 0 for masked scores).
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = __fadd_rn(x, 12582912.f);
+  const float j = __fsub_rn(t, 12582912.f);
+  const float f = __fsub_rn(x, j);
+  const float p = fmaf(fmaf(fmaf(kExpC3, f, kExpC2), f, kExpC1), f, kExpC0);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Two non-negative finite fp32 -> bf16x2 (low half = lo) with integer ops:
+// add half an ulp of bf16, keep the high 16 bits of each (round half up).
+__device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo) + 0x8000u;
+  const uint32_t b = __float_as_uint(hi) + 0x8000u;
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 template <int D>
 struct AttnCfg {
   static constexpr int kTileBytes = kBM * D * 2;          // one 128 x D bf16 tile
@@ -49,8 +108,8 @@ struct AttnCfg {
   static constexpr int kKVOff = 2 * kTileBytes;
   static constexpr int kBarOff = kKVOff + kStages * kTileBytes;
   // q_full, kv_full[kStages], kv_empty[kStages], s_full[2], p_full[2],
-  // o_full[2], drain
-  static constexpr int kNumBars = 1 + 2 * kStages + 7;
+  // o_full[2], drain, turn[2]
+  static constexpr int kNumBars = 1 + 2 * kStages + 9;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem base, abort flag
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + alignment slack
   // TMEM column of S_t (P_t aliases its first 64 columns) and of O_t.
@@ -66,7 +125,26 @@ struct AttnParams {
   __nv_bfloat16* o;
   int64_t o_sb, o_sh, o_ss;
   int* status;
+  unsigned long long* trace;   // timeline buffer (trace builds only), else null
 };
+
+// Optional timeline instrumentation (compiled out unless FA_ATTN_TRACE):
+// clock64() stamps per CTA for the first kTraceCtas CTAs, slot layout
+// [cta][iteration j][event], events 6t+0..6t+5 softmax tile t (wait start,
+// S ready, row max done, exp turn acquired, exps done, P stored + arrived),
+// 12+2t / 13+2t MMA tile t (P seen, S issued).
+constexpr int kTraceCtas = 8;
+constexpr int kTraceEvents = 16;
+constexpr int kTraceIters = 64;
+#ifdef FA_ATTN_TRACE
+#define FA_TRACE(j, ev)                                                              \
+  do {                                                                               \
+    if (p.trace != nullptr && blockIdx.x < kTraceCtas && (j) < kTraceIters)          \
+      p.trace[(blockIdx.x * kTraceIters + (j)) * kTraceEvents + (ev)] = clock64();   \
+  } while (0)
+#else
+#define FA_TRACE(j, ev) do { } while (0)
+#endif
 
 // Bounded drain wait used only on the abort path: returns when the phase
 // completes or after a short limit, ignoring the abort flag.
@@ -83,6 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using C = AttnCfg<D>;
+  constexpr int kEmuMod = (D == 64) ? FA_ATTN_EMU_MOD_D64 : FA_ATTN_EMU_MOD_D128;
+  constexpr bool kPackAlu = FA_ATTN_PACK_ALU != 0;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -97,6 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar_p_full = [&](int t) { return bars + 8u * (3 + 2 * C::kStages + t); };
   auto bar_o_full = [&](int t) { return bars + 8u * (5 + 2 * C::kStages + t); };
   const uint32_t bar_drain = bars + 8u * (7 + 2 * C::kStages);
+  // turn[t] completes each time the other softmax warpgroup ends an exp phase.
+  auto bar_turn = [&](int t) { return bars + 8u * (8 + 2 * C::kStages + t); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + C::kMiscOff + 4);
 
@@ -133,6 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_o_full(t), 1);
     }
     mbar_init(bar_drain, 1);
+    mbar_init(bar_turn(0), kBM);
+    mbar_init(bar_turn(1), kBM);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -150,6 +234,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp >= 8) {
+    // Warpgroup 2: producer, MMA issuer, two idle warps.
+#if FA_ATTN_SETMAXNREG
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+#endif
   if (warp == 8) {
     // =================== TMA producer ===================
     if (elect_one()) {
@@ -214,6 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
+            FA_TRACE(j - 1, 12 + 2 * t);
             const uint32_t vbase = sKV + vslot * C::kTileBytes;
 #pragma unroll
             for (int kk = 0; kk < kBN / 16; ++kk) {
@@ -234,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      sdesc_sw128(kbase + off, 16, 1024), kIdQK, kk > 0 ? 1u : 0u);
             }
             mma_commit(bar_s_full(t));
+            FA_TRACE(j, 13 + 2 * t);
           }
         }
         if (!ok) break;
@@ -254,7 +345,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       drain_wait(bar_drain, 0);
     }
     __syncwarp();
-  } else if (warp < 8) {
+  }
+  } else {
+#if FA_ATTN_SETMAXNREG
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+#endif
     // =================== softmax / correction / epilogue ===================
     const int t = warp >> 2;
     const int wq = warp & 3;
@@ -268,14 +363,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.f;             // running row sum of exp2(s * sl2 - m_ref)
     bool ok = true;
     const int q_tile0 = q0 + t * kBM;
+    const bool pingpong = (FA_ATTN_PINGPONG != 0) && nt[0] > 0 && nt[1] > 0;
     for (int j = 0; j < nt[t]; ++j) {
+      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 0);
       if (!mbar_wait(bar_s_full(t), j & 1, abort_flag, p.status)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 1);
       uint32_t sr[128];
-      tmem_ld128_wait(tS, sr);
+      {
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld4x32_wait(tS, r0, r1, r2, r3);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          sr[i] = r0[i];
+          sr[32 + i] = r1[i];
+          sr[64 + i] = r2[i];
+          sr[96 + i] = r3[i];
+        }
+      }
       const int k0 = j * kBN;
       const bool need_mask = (k0 + kBN > p.S) || (CAUSAL && (k0 + kBN - 1 > q_tile0));
       if (need_mask) {
@@ -284,9 +392,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < kBN; ++c)
           if (k0 + c >= lim) sr[c] = __float_as_uint(-INFINITY);
       }
-      float mx = __uint_as_float(sr[0]);
+      // Row max as four independent chains of 3-input maxima (short latency).
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      for (int c = 0; c < kBN; c += 8)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          mx4[i] = fmax3(mx4[i], __uint_as_float(sr[c + 2 * i]), __uint_as_float(sr[c + 2 * i + 1]));
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       const float m_blk = mx * sl2;
       const float m_new = fmaxf(m_ref, m_blk);
       const bool need = (m_new - m_ref) > kRescaleThreshold;
@@ -307,22 +420,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= alpha;
         m_ref = m_use;
       }
+      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 2);
+      // Exp phases alternate between the two warpgroups (tile 0 first) so
+      // each has the SM's MUFU throughput to itself while the tensor core
+      // works on the other tile.  Tile 0's turn j follows tile 1's turn j-1;
+      // tile 1's turn j follows tile 0's turn j.
+      if (pingpong && (t == 1 || j > 0) &&
+          !mbar_wait(bar_turn(t), t == 0 ? ((j - 1) & 1) : (j & 1), abort_flag, p.status)) {
+        ok = false;
+        break;
+      }
+      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 3);
       const float neg_m = -m_ref;
-      float rs0 = 0.f, rs1 = 0.f;
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[64];
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * c]), sl2, neg_m));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * c + 1]), sl2, neg_m));
-        rs0 += p0;
-        rs1 += p1;
-        pk[c] = pack_bf16x2(p0, p1);
+        const float x0 = fmaf(__uint_as_float(sr[2 * c]), sl2, neg_m);
+        const float x1 = fmaf(__uint_as_float(sr[2 * c + 1]), sl2, neg_m);
+        // A fixed share of the pairs goes to the FMA pipe, the rest to MUFU.
+        const bool emu = (kEmuMod > 0) && (c % (kEmuMod > 0 ? kEmuMod : 1) == kEmuMod - 1);
+        const float p0 = emu ? exp2_fma(x0) : ex2_approx(x0);
+        const float p1 = emu ? exp2_fma(x1) : ex2_approx(x1);
+        rs[c & 3] += p0 + p1;
+        pk[c] = kPackAlu ? pack_bf16x2_alu(p0, p1) : pack_bf16x2(p0, p1);
       }
-      l += rs0 + rs1;
+      if (pingpong) mbar_arrive(bar_turn(1 - t));
+      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 4);
+      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       tmem_st64(tS, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_p_full(t));
+      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 5);
+    }
+    // Causal units give tile 0 one block fewer than tile 1: pass the turn for
+    // tile 1's last block without work.
+    if (ok && pingpong && t == 0 && nt[0] < nt[1]) {
+      if (mbar_wait(bar_turn(0), (nt[0] - 1) & 1, abort_flag, p.status))
+        mbar_arrive(bar_turn(1));
+      else
+        ok = false;
     }
     if (ok && nt[t] > 0 && mbar_wait(bar_o_full(t), 0, abort_flag, p.status)) {
       tc_fence_after();
@@ -379,6 +517,20 @@ int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
 }  // namespace
 }  // namespace fa
 
+namespace fa {
+namespace {
+unsigned long long* g_trace_buffer = nullptr;
+}
+}  // namespace fa
+
+#ifdef FA_ATTN_TRACE
+// Trace builds only: device buffer of kTraceCtas * kTraceIters * kTraceEvents
+// 64-bit stamps that subsequent fa_attn_fwd launches fill.
+extern "C" void fa_attn_set_trace_buffer(void* buf) {
+  fa::g_trace_buffer = static_cast<unsigned long long*>(buf);
+}
+#endif
+
 extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int H,
                            int S, int D, const int64_t* st, int causal, float scale,
                            void* stream) {
@@ -417,6 +569,7 @@ extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o,
   prm.o_sh = st[13];
   prm.o_ss = st[14];
   prm.status = device_status_ptr();
+  prm.trace = g_trace_buffer;
   if (prm.status == nullptr) return FA_ERR_CUDA;
   const int grid = static_cast<int>(units);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
