@@ -120,6 +120,7 @@ struct AttnCfg {
 struct AttnParams {
   int B, H, S;
   int n_units_per_head;   // ceil(S / 256)
+  int group_heads;        // (batch, head) pairs per scheduling group
   int nkv;                // ceil(S / 128)
   float scale_log2;       // scale * log2(e)
   __nv_bfloat16* o;
@@ -185,9 +186,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // ---- work unit: (batch, head) major, longest causal unit first ----------
-  const int bh = blockIdx.x / p.n_units_per_head;
-  int qu = blockIdx.x - bh * p.n_units_per_head;
+  // ---- work unit ------------------------------------------------------------
+  // (batch, head) pairs are taken in groups of p.group_heads (K/V of a group
+  // stay resident in L2).  Inside a group the units run query-position-major,
+  // and for causal attention the longest (last) query units of every head of
+  // the group go first, so the short units fill the tail.
+  const int group_units = p.group_heads * p.n_units_per_head;
+  const int grp = blockIdx.x / group_units;
+  const int r_in = blockIdx.x - grp * group_units;
+  const int heads_here = min(p.group_heads, p.B * p.H - grp * p.group_heads);
+  int qu = r_in / heads_here;
+  const int bh = grp * p.group_heads + (r_in - qu * heads_here);
   if (CAUSAL) qu = p.n_units_per_head - 1 - qu;
   const int b = bh / p.H;
   const int h = bh - b * p.H;
@@ -562,6 +571,14 @@ extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o,
   prm.H = H;
   prm.S = S;
   prm.n_units_per_head = (S + 2 * kBM - 1) / (2 * kBM);
+  // Group size: about 64 MiB of K/V per group (half the 126 MB L2), >= 1.
+  {
+    const int64_t kv_bytes_per_head = 2ll * S * D * 2;
+    int64_t g = (64ll << 20) / (kv_bytes_per_head > 0 ? kv_bytes_per_head : 1);
+    if (g < 1) g = 1;
+    if (g > static_cast<int64_t>(B) * H) g = static_cast<int64_t>(B) * H;
+    prm.group_heads = static_cast<int>(g);
+  }
   prm.nkv = (S + kBN - 1) / kBN;
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.o = static_cast<__nv_bfloat16*>(o);
