@@ -30,6 +30,7 @@ SIGNATURES = {
                              _c_int, _vp]),
     "fa_mlp_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp]),
     "fa_device_status": (_c_int, []),
+    "fa_selftest_wait_timeout": (_c_int, [_c_int, _vp]),
 }
 
 _lock = threading.Lock()

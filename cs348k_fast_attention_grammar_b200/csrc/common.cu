@@ -103,6 +103,39 @@ int make_tmap_bhsd(CUtensorMap* map, const void* base, int B, int H, int S, int 
 
 }  // namespace fa
 
+namespace fa {
+namespace {
+
+// One CTA waits on an mbarrier that nothing ever arrives on.  The bounded wait
+// gives up after limit_ns, raises the CTA abort flag and records kDevTimeout
+// in the device status word; the kernel then returns normally.
+__global__ void wait_timeout_probe(int* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  mbar_wait_limit(smem_u32(&bar), 0, &abort_flag, status, limit_ns);
+}
+
+}  // namespace
+}  // namespace fa
+
+extern "C" int fa_selftest_wait_timeout(int limit_us, void* stream) {
+  if (limit_us <= 0 || limit_us > 1000000) return FA_ERR_ARG;
+  int dev = 0;
+  int rc = fa::prepare_device(nullptr, 0, &dev);
+  if (rc != FA_OK) return rc;
+  int* status = fa::device_status_ptr();
+  if (status == nullptr) return FA_ERR_CUDA;
+  fa::wait_timeout_probe<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      status, static_cast<unsigned long long>(limit_us) * 1000ull);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
 extern "C" const char* fa_strerror(int status) {
   switch (status) {
     case FA_OK: return "success";

@@ -87,25 +87,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Polling back-off between failed checks of a bounded wait (0 = spin).
+#ifndef FA_WAIT_BACKOFF_NS
+#define FA_WAIT_BACKOFF_NS 0
+#endif
+
 // Bounded wait for the phase with the given parity to complete.  Returns false
 // when the CTA-wide abort flag is raised (by this or another warp) or when the
 // wait exceeds kWaitLimitNs; in the latter case it raises the abort flag and
 // records kDevTimeout in *status.  Callers unwind to the common teardown.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
-                                          volatile int* abort_flag, int* status) {
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity,
+                                                volatile int* abort_flag, int* status,
+                                                unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
+#if FA_WAIT_BACKOFF_NS > 0
+    __nanosleep(FA_WAIT_BACKOFF_NS);
+#endif
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 31u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         atomicExch(status, kDevTimeout);
         return false;
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          volatile int* abort_flag, int* status) {
+  return mbar_wait_limit(bar, parity, abort_flag, status, kWaitLimitNs);
 }
 
 // ----------------------------------------------------------------------------

@@ -119,6 +119,18 @@ int fa_mlp_fwd_noalloc(const void* x, const void* w1, const void* w2, void* y, i
                        int N, int act, void* stream);
 
 /*
+ * Failure-detection self test: launches one CTA that waits on an mbarrier no
+ * one ever arrives on, with a limit of limit_us microseconds (1 .. 10^6).  The
+ * bounded wait gives up, records FA_ERR_TIMEOUT in the device status word and
+ * the kernel returns normally (no trap, no fault), so the context stays
+ * usable; read the result with fa_device_status().  Every wait inside the
+ * library's kernels is bounded the same way (limit 1 s).  Reference analog:
+ * the search's compile timeout (grammar/optimization.py:57-62,267-280), which
+ * turns a hung compile into a recorded failure.
+ */
+int fa_selftest_wait_timeout(int limit_us, void* stream);
+
+/*
  * Reads and clears the device-side status word of the current device
  * (FA_OK, or FA_ERR_TIMEOUT when a kernel's bounded wait ran out).
  * Synchronises the device.

@@ -76,6 +76,7 @@ def test_argument_checks_without_device():
     assert lib.fa_gemm_act(p, p, p, 128, 128, 64, 64, 128, 128, 7, None) == codes["FA_ERR_ARG"]
     assert lib.fa_gemm_act(p, p, p, 128, 128, 64, 60, 128, 128, 0, None) == \
         codes["FA_ERR_STRIDE"]
+    assert lib.fa_selftest_wait_timeout(0, None) == codes["FA_ERR_ARG"]
     fn = lib.fa_mlp_fwd_noalloc
     fn.restype = ctypes.c_int
     fn.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
