@@ -444,7 +444,8 @@ def attention_e2e(args, fab, cfg, q, k, v, world, device, flops_total):
     return {"value": flops_total / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
             "steps": steps, "h2d_bytes_per_step": 3 * q.numel() * 2 * world,
             "d2h_bytes_per_step": q.numel() * 2 * world,
-            "path": "attention_from_host (pinned host -> device -> host)"}
+            "path": "attention_from_host: pinned host -> device -> host, (batch, head) pairs "
+                    "in 8 chunks pipelined over copy-in / kernel / copy-out streams"}
 
 
 def bench_mlp(args, fab, device, world, rank):

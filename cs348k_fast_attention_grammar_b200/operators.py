@@ -101,14 +101,18 @@ def attention_from_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                         causal: bool = False, scale: float | None = None,
                         out: torch.Tensor | None = None,
                         device: torch.device | int | str | None = None,
-                        workspace: dict | None = None) -> torch.Tensor:
-    """``attention`` for host tensors: H2D copy of q, k, v, the fused kernel,
-    D2H copy of O, all enqueued on the current stream of ``device``.
+                        workspace: dict | None = None, chunks: int = 8) -> torch.Tensor:
+    """``attention`` for ``[B, H, S, D]`` host tensors: host-to-device copy of
+    q, k, v, the fused kernel, device-to-host copy of O.
 
-    Host tensors should be pinned for the copies to be asynchronous.  The
-    result lands in ``out`` (a host tensor, allocated pinned if omitted); the
-    caller synchronises the stream before reading it.  ``workspace`` (a dict)
-    keeps the device buffers between calls.
+    The (batch, head) pairs are split into ``chunks`` groups that flow through
+    three streams -- copies in, kernel, copies out -- chained by events, so
+    the two PCIe directions and the kernels overlap; the current stream of
+    ``device`` waits for the last copy out, so work ordered after the call on
+    that stream (or a synchronize) sees the whole result.  Host tensors should
+    be pinned and contiguous for the copies to be asynchronous.  The result
+    lands in ``out`` (allocated pinned if omitted).  ``workspace`` (a dict)
+    keeps the device buffers, streams and events between calls.
     """
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None \
         else torch.device(device)
@@ -117,20 +121,51 @@ def attention_from_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     for name, t in (("q", q), ("k", k), ("v", v)):
         if t.is_cuda or t.dtype != _BF16:
             raise ValueError(f"{name} must be a bfloat16 host tensor")
+        if t.dim() != 4 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous 4-D [B, H, S, D] tensor")
+    B, H, S, D = q.shape
+    pairs = B * H
+    nch = max(1, min(int(chunks), pairs))
+    bounds = [pairs * i // nch for i in range(nch + 1)]
     ws = workspace if workspace is not None else {}
-    key = (tuple(q.shape), dev)
+    key = (tuple(q.shape), dev, nch)
     if ws.get("key") != key:
+        for st in ws.get("streams", ()):
+            st.synchronize()          # the old buffers may still be in use
         ws.clear()
         ws["key"] = key
         for name in ("q", "k", "v", "o"):
-            ws[name] = torch.empty(q.shape, dtype=_BF16, device=dev)
-    ws["q"].copy_(q, non_blocking=True)
-    ws["k"].copy_(k, non_blocking=True)
-    ws["v"].copy_(v, non_blocking=True)
-    attention(ws["q"], ws["k"], ws["v"], causal=causal, scale=scale, out=ws["o"])
+            ws[name] = torch.empty((1, pairs, S, D), dtype=_BF16, device=dev)
+        ws["streams"] = [torch.cuda.Stream(device=dev) for _ in range(3)]
+        ws["ev_in"] = [torch.cuda.Event() for _ in range(nch)]
+        ws["ev_cmp"] = [torch.cuda.Event() for _ in range(nch)]
+        ws["ev_out"] = torch.cuda.Event()
     if out is None:
         out = torch.empty(q.shape, dtype=_BF16, pin_memory=True)
-    out.copy_(ws["o"], non_blocking=True)
+    s_in, s_cmp, s_out = ws["streams"]
+    cur = torch.cuda.current_stream(dev)
+    # the previous call's consumers of the buffers are ordered before us
+    s_in.wait_stream(cur)
+    s_cmp.wait_stream(cur)
+    s_out.wait_stream(cur)
+    hq, hk, hv, ho = (t.view(1, pairs, S, D) for t in (q, k, v, out))
+    for c in range(nch):
+        a, z = bounds[c], bounds[c + 1]
+        with torch.cuda.stream(s_in):
+            ws["q"][:, a:z].copy_(hq[:, a:z], non_blocking=True)
+            ws["k"][:, a:z].copy_(hk[:, a:z], non_blocking=True)
+            ws["v"][:, a:z].copy_(hv[:, a:z], non_blocking=True)
+            ws["ev_in"][c].record(s_in)
+        s_cmp.wait_event(ws["ev_in"][c])
+        with torch.cuda.stream(s_cmp):
+            attention(ws["q"][:, a:z], ws["k"][:, a:z], ws["v"][:, a:z], causal=causal,
+                      scale=scale, out=ws["o"][:, a:z])
+            ws["ev_cmp"][c].record(s_cmp)
+        s_out.wait_event(ws["ev_cmp"][c])
+        with torch.cuda.stream(s_out):
+            ho[:, a:z].copy_(ws["o"][:, a:z], non_blocking=True)
+    ws["ev_out"].record(s_out)
+    cur.wait_event(ws["ev_out"])
     return out
 
 

@@ -83,12 +83,18 @@ def test_bshd_layout_is_bit_identical():
     assert torch.equal(o1.permute(0, 2, 1, 3), o2)
 
 
-def test_from_host_matches_device_call():
-    q, k, v = (_rand((1, 2, 256, 64), 30 + i).pin_memory() for i in range(3))
-    o_host = attention_from_host(q, k, v, causal=False, device=DEV)
-    torch.cuda.synchronize()
-    o_dev = attention(q.to(DEV), k.to(DEV), v.to(DEV))
-    assert torch.equal(o_host, o_dev.cpu())
+@pytest.mark.parametrize("chunks", [1, 2, 8])
+def test_from_host_matches_device_call(chunks):
+    """Chunked, stream-pipelined host path == one device call, bit for bit
+    (3 pairs: chunk counts above the pair count are clamped)."""
+    q, k, v = (_rand((1, 3, 384, 128), 30 + i).pin_memory() for i in range(3))
+    ws = {}
+    for _ in range(2):                       # reuses the workspace on the 2nd call
+        o_host = attention_from_host(q, k, v, causal=True, device=DEV, workspace=ws,
+                                     chunks=chunks)
+        torch.cuda.synchronize()
+        o_dev = attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=True)
+        assert torch.equal(o_host, o_dev.cpu())
 
 
 def test_repeated_calls_are_deterministic():
