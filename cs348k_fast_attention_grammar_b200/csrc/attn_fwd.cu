@@ -53,6 +53,11 @@ constexpr float kRescaleThreshold = 8.0f;
 #ifndef FA_ATTN_PACK_ALU
 #define FA_ATTN_PACK_ALU 0
 #endif
+// 1 = P is published in two halves (keys 0-63, 64-127) so the first half of
+// O += P V starts while the softmax computes the second half.
+#ifndef FA_ATTN_SPLIT_P
+#define FA_ATTN_SPLIT_P 1
+#endif
 // 1 = the two softmax warpgroups take turns on their exp phases.
 #ifndef FA_ATTN_PINGPONG
 #define FA_ATTN_PINGPONG 1
@@ -108,8 +113,8 @@ struct AttnCfg {
   static constexpr int kKVOff = 2 * kTileBytes;
   static constexpr int kBarOff = kKVOff + kStages * kTileBytes;
   // q_full, kv_full[kStages], kv_empty[kStages], s_full[2], p_full[2],
-  // o_full[2], drain, turn[2]
-  static constexpr int kNumBars = 1 + 2 * kStages + 9;
+  // o_full[2], drain, turn[2], p_half[2]
+  static constexpr int kNumBars = 1 + 2 * kStages + 11;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem base, abort flag
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + alignment slack
   // TMEM column of S_t (P_t aliases its first 64 columns) and of O_t.
@@ -180,6 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bar_drain = bars + 8u * (7 + 2 * C::kStages);
   // turn[t] completes each time the other softmax warpgroup ends an exp phase.
   auto bar_turn = [&](int t) { return bars + 8u * (8 + 2 * C::kStages + t); };
+  // p_half[t] completes when the first 64 keys of P_t are in TMEM.
+  auto bar_p_half = [&](int t) { return bars + 8u * (10 + 2 * C::kStages + t); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + C::kMiscOff + 4);
 
@@ -221,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar_s_full(t), 1);
       mbar_init(bar_p_full(t), kBM);
+      mbar_init(bar_p_half(t), kBM);
       mbar_init(bar_o_full(t), 1);
     }
     mbar_init(bar_drain, 1);
@@ -307,19 +315,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j >= 1 && j - 1 < nt[t]) {
             // O_t += P_t(j-1) V_{j-1}: A = P from TMEM (8 columns per K=16 step),
             // B = V tile, MN-major (d contiguous), 64-wide d atoms 16 KiB apart.
-            if (!mbar_wait(bar_p_full(t), (j - 1) & 1, abort_flag, p.status)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            FA_TRACE(j - 1, 12 + 2 * t);
             const uint32_t vbase = sKV + vslot * C::kTileBytes;
 #pragma unroll
-            for (int kk = 0; kk < kBN / 16; ++kk) {
-              const uint64_t bdesc = sdesc_sw128(vbase + kk * 2048, 16384, 1024);
-              mma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8, bdesc, kIdPV,
-                     (j - 1 > 0 || kk > 0) ? 1u : 0u);
+            for (int half = 0; half < 2; ++half) {
+              // With split publication, keys 0-63 (K steps 0-3) go as soon as
+              // the first half of P is stored, keys 64-127 after the rest.
+              if (half == 0 && !FA_ATTN_SPLIT_P) continue;
+              const uint32_t bar = (half == 0) ? bar_p_half(t) : bar_p_full(t);
+              if (!mbar_wait(bar, (j - 1) & 1, abort_flag, p.status)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              if (half == 1) FA_TRACE(j - 1, 12 + 2 * t);
+              const int kk0 = (FA_ATTN_SPLIT_P && half == 1) ? kBN / 32 : 0;
+              const int kk1 = (half == 0) ? kBN / 32 : kBN / 16;
+#pragma unroll
+              for (int kk = kk0; kk < kk1; ++kk) {
+                const uint64_t bdesc = sdesc_sw128(vbase + kk * 2048, 16384, 1024);
+                mma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8, bdesc, kIdPV,
+                       (j - 1 > 0 || kk > 0) ? 1u : 0u);
+              }
             }
+            if (!ok) break;
             if (j - 1 == nt[t] - 1) mma_commit(bar_o_full(t));
           }
           if (j < nt[t]) {
@@ -442,22 +460,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 3);
       const float neg_m = -m_ref;
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[64];
+      uint32_t pk[2][32];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float x0 = fmaf(__uint_as_float(sr[2 * c]), sl2, neg_m);
-        const float x1 = fmaf(__uint_as_float(sr[2 * c + 1]), sl2, neg_m);
-        // A fixed share of the pairs goes to the FMA pipe, the rest to MUFU.
-        const bool emu = (kEmuMod > 0) && (c % (kEmuMod > 0 ? kEmuMod : 1) == kEmuMod - 1);
-        const float p0 = emu ? exp2_fma(x0) : ex2_approx(x0);
-        const float p1 = emu ? exp2_fma(x1) : ex2_approx(x1);
-        rs[c & 3] += p0 + p1;
-        pk[c] = kPackAlu ? pack_bf16x2_alu(p0, p1) : pack_bf16x2(p0, p1);
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int cc = 0; cc < 32; ++cc) {
+          const int c = half * 32 + cc;
+          const float x0 = fmaf(__uint_as_float(sr[2 * c]), sl2, neg_m);
+          const float x1 = fmaf(__uint_as_float(sr[2 * c + 1]), sl2, neg_m);
+          // A fixed share of the pairs goes to the FMA pipe, the rest to MUFU.
+          const bool emu = (kEmuMod > 0) && (c % (kEmuMod > 0 ? kEmuMod : 1) == kEmuMod - 1);
+          const float p0 = emu ? exp2_fma(x0) : ex2_approx(x0);
+          const float p1 = emu ? exp2_fma(x1) : ex2_approx(x1);
+          rs[c & 3] += p0 + p1;
+          pk[half][cc] = kPackAlu ? pack_bf16x2_alu(p0, p1) : pack_bf16x2(p0, p1);
+        }
+        if (FA_ATTN_SPLIT_P && half == 0) {
+          // keys 0-63 of P -> TMEM columns [0, 32); the MMA warp starts on them
+          tmem_st32(tS, pk[0]);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar_p_half(t));
+        }
       }
       if (pingpong) mbar_arrive(bar_turn(1 - t));
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 4);
       l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
-      tmem_st64(tS, pk);
+      if (!FA_ATTN_SPLIT_P) tmem_st32(tS, pk[0]);
+      tmem_st32(tS + 32, pk[1]);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_p_full(t));
