@@ -58,9 +58,12 @@ constexpr float kRescaleThreshold = 8.0f;
 #ifndef FA_ATTN_SPLIT_P
 #define FA_ATTN_SPLIT_P 1
 #endif
-// 1 = the two softmax warpgroups take turns on their exp phases.
-#ifndef FA_ATTN_PINGPONG
-#define FA_ATTN_PINGPONG 1
+// 1 = the two softmax warpgroups take turns on their exp phases (per D).
+#ifndef FA_ATTN_PINGPONG_D64
+#define FA_ATTN_PINGPONG_D64 1
+#endif
+#ifndef FA_ATTN_PINGPONG_D128
+#define FA_ATTN_PINGPONG_D128 0
 #endif
 // 1 = move registers from the producer/MMA warpgroup (56 per thread) to the
 // two softmax warpgroups (224 per thread) with setmaxnreg.  The split adds up
@@ -390,7 +393,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.f;             // running row sum of exp2(s * sl2 - m_ref)
     bool ok = true;
     const int q_tile0 = q0 + t * kBM;
-    const bool pingpong = (FA_ATTN_PINGPONG != 0) && nt[0] > 0 && nt[1] > 0;
+    constexpr bool kPingPong = (D == 64) ? (FA_ATTN_PINGPONG_D64 != 0) : (FA_ATTN_PINGPONG_D128 != 0);
+    const bool pingpong = kPingPong && nt[0] > 0 && nt[1] > 0;
     for (int j = 0; j < nt[t]; ++j) {
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 0);
       if (!mbar_wait(bar_s_full(t), j & 1, abort_flag, p.status)) {
