@@ -7,6 +7,7 @@ through its C ABI, ``include/fa_b200.h``; there is no fallback path):
     attention_bshd(q, k, v, causal=False)                    # (B, S, H, D) layout
     attention_from_host(q, k, v, causal=False, ...)          # pinned host tensors
     mlp(x, w1, w2, act="gelu_tanh")                          # act(x@w1)@w2
+    mlp_ln(x, w1, w2)                                        # LN(relu(x@w1)@w2 + x)
     gemm_act(a, b, act="none")                               # act(a@b)
 
 ``kernel_module`` exposes the reference's ``fn(KT, Q, V)`` + ``KERNEL_META``
@@ -20,8 +21,11 @@ from .operators import (  # noqa: F401
     attention_from_host,
     device_status,
     gemm_act,
+    layer_norm_rows,
     mlp,
+    mlp_ln,
 )
 
-__all__ = ["attention", "attention_bshd", "attention_from_host", "mlp", "gemm_act",
+__all__ = ["attention", "attention_bshd", "attention_from_host", "mlp", "mlp_ln",
+           "layer_norm_rows", "gemm_act",
            "device_status", "FaError", "load", "lib_path"]

@@ -29,6 +29,9 @@ SIGNATURES = {
     "fa_gemm_act": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _i64, _i64, _i64,
                              _c_int, _vp]),
     "fa_mlp_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp]),
+    "fa_mlp_ln_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
+                               _c_float, _vp]),
+    "fa_layernorm_rows": (_c_int, [_vp, _vp, _c_int, _c_int, _i64, _i64, _c_float, _vp]),
     "fa_device_status": (_c_int, []),
     "fa_selftest_wait_timeout": (_c_int, [_c_int, _vp]),
 }

@@ -45,6 +45,8 @@ struct GemmParams {
   int act;
   __nv_bfloat16* c;
   int64_t ldc;
+  const __nv_bfloat16* res;   // optional residual added after the activation
+  int64_t ldr;
   int* status;
 };
 
@@ -207,11 +209,27 @@ __global__ void __launch_bounds__(kGThreads, 1)
       for (int c = 0; c < kGBN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32_wait(tmem + lane_off + 256u * acc + c * 32, r);
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = apply_act(__uint_as_float(r[e]), p.act);
+        if (p.res != nullptr && row < p.M && tn * kGBN + c * 32 < p.N) {
+          // residual: 32 bf16 of the same row and columns, added in fp32
+          const uint4* rs = reinterpret_cast<const uint4*>(
+              p.res + static_cast<int64_t>(row) * p.ldr + tn * kGBN + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 u = __ldg(rs + q);
+            const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              v[8 * q + 2 * e] += __uint_as_float(ws[e] << 16);
+              v[8 * q + 2 * e + 1] += __uint_as_float(ws[e] & 0xffff0000u);
+            }
+          }
+        }
         uint32_t w[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          w[e] = pack_bf16x2(apply_act(__uint_as_float(r[2 * e]), p.act),
-                             apply_act(__uint_as_float(r[2 * e + 1]), p.act));
+        for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
         if (row < p.M && tn * kGBN + c * 32 < p.N) {
           uint4* dst = reinterpret_cast<uint4*>(crow + c * 32);
           dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -237,7 +255,8 @@ int g_num_sms[64] = {};
 bool g_gemm_attr[64] = {};
 
 int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int64_t lda,
-                int64_t ldb, int64_t ldc, int act, cudaStream_t stream) {
+                int64_t ldb, int64_t ldc, int act, cudaStream_t stream,
+                const void* res = nullptr, int64_t ldr = 0) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FA_ERR_CUDA;
   if (!g_gemm_attr[dev]) {
@@ -261,6 +280,8 @@ int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int6
   p.act = act;
   p.c = static_cast<__nv_bfloat16*>(c);
   p.ldc = ldc;
+  p.res = static_cast<const __nv_bfloat16*>(res);
+  p.ldr = ldr;
   p.status = device_status_ptr();
   if (p.status == nullptr) return FA_ERR_CUDA;
   const int grid = min(p.num_tiles, g_num_sms[dev] > 0 ? g_num_sms[dev] : 148);
@@ -337,6 +358,142 @@ extern "C" int fa_mlp_fwd_noalloc(const void* x, const void* w1, const void* w2,
   rc = fa::launch_gemm(x, w1, hidden, M, N, K, K, N, N, act, s);
   if (rc != FA_OK) return rc;
   return fa::launch_gemm(hidden, w2, y, M, K, N, N, K, K, FA_ACT_NONE, s);
+}
+
+// ---------------------------------------------------------------------------
+// Row LayerNorm without affine parameters, out = (r - mean) / sqrt(var + eps)
+// over each row of r (the reference block's last stage,
+// run_mlp_search.py:76-93, checked by its verify at :146-149).  One CTA of
+// 256 threads per row; the row stays in registers (8 bf16 per 16-byte load),
+// so mean and variance are two exact passes over registers.  HBM bound:
+// 2 bytes read + 2 bytes written per element.
+// ---------------------------------------------------------------------------
+namespace fa {
+namespace {
+
+constexpr int kLnThreads = 256;
+constexpr int kLnVec = 4;                                   // uint4 per thread
+constexpr int kLnMaxN = kLnThreads * 8 * kLnVec;           // 8192
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float t = (threadIdx.x < kLnThreads / 32) ? red[threadIdx.x] : 0.f;
+  if (w == 0) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+__global__ void __launch_bounds__(kLnThreads)
+    layernorm_rows_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, int N, int64_t ld_in,
+                          int64_t ld_out, float eps) {
+  __shared__ float red[kLnThreads / 32];
+  const int64_t row = blockIdx.x;
+  const uint4* src = reinterpret_cast<const uint4*>(in + row * ld_in);
+  float x[kLnVec][8];
+  float s = 0.f;
+#pragma unroll
+  for (int v = 0; v < kLnVec; ++v) {
+    const int idx = (v * kLnThreads + threadIdx.x) * 8;
+    if (idx < N) {
+      const uint4 u = src[v * kLnThreads + threadIdx.x];
+      const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        x[v][2 * e] = __uint_as_float(ws[e] << 16);
+        x[v][2 * e + 1] = __uint_as_float(ws[e] & 0xffff0000u);
+        s += x[v][2 * e] + x[v][2 * e + 1];
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[v][e] = 0.f;
+    }
+  }
+  const float mean = block_sum(s, red) / static_cast<float>(N);
+  float q = 0.f;
+#pragma unroll
+  for (int v = 0; v < kLnVec; ++v) {
+    const int idx = (v * kLnThreads + threadIdx.x) * 8;
+    if (idx < N) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = x[v][e] - mean;
+        q = fmaf(d, d, q);
+      }
+    }
+  }
+  const float var = block_sum(q, red) / static_cast<float>(N);
+  const float inv = rsqrtf(var + eps);
+  uint4* dst = reinterpret_cast<uint4*>(out + row * ld_out);
+#pragma unroll
+  for (int v = 0; v < kLnVec; ++v) {
+    const int idx = (v * kLnThreads + threadIdx.x) * 8;
+    if (idx < N) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        w[e] = pack_bf16x2((x[v][2 * e] - mean) * inv, (x[v][2 * e + 1] - mean) * inv);
+      dst[v * kLnThreads + threadIdx.x] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+int check_ln_args(const void* in, const void* out, int M, int N, int64_t ld_in, int64_t ld_out,
+                  float eps) {
+  if (!in || !out) return FA_ERR_NULL;
+  if (M <= 0 || N <= 0 || (N % 8) != 0 || N > kLnMaxN) return FA_ERR_SHAPE;
+  if (ld_in < N || ld_out < N) return FA_ERR_STRIDE;
+  if ((ld_in % 8) || (ld_out % 8)) return FA_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) % 16) return FA_ERR_ALIGN;
+  if (!(eps > 0.f)) return FA_ERR_ARG;
+  return FA_OK;
+}
+
+int launch_ln(const void* in, void* out, int M, int N, int64_t ld_in, int64_t ld_out, float eps,
+              cudaStream_t stream) {
+  int dev = 0;
+  int rc = prepare_device(nullptr, 0, &dev);
+  if (rc != FA_OK) return rc;
+  layernorm_rows_kernel<<<M, kLnThreads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), N, ld_in, ld_out,
+      eps);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
+}  // namespace
+}  // namespace fa
+
+extern "C" int fa_layernorm_rows(const void* in, void* out, int M, int N, int64_t ld_in,
+                                 int64_t ld_out, float eps, void* stream) {
+  const int rc = fa::check_ln_args(in, out, M, N, ld_in, ld_out, eps);
+  if (rc != FA_OK) return rc;
+  return fa::launch_ln(in, out, M, N, ld_in, ld_out, eps, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fa_mlp_ln_fwd(const void* x, const void* w1, const void* w2, void* hidden,
+                             void* resid, void* out, int M, int K, int N, float eps,
+                             void* stream) {
+  // hidden = relu(x @ w1); resid = hidden @ w2 + x; out = LayerNorm(resid)
+  int rc = fa::check_gemm_args(x, w1, hidden, M, N, K, K, N, N, FA_ACT_RELU);
+  if (rc != FA_OK) return rc;
+  rc = fa::check_gemm_args(hidden, w2, resid, M, K, N, N, K, K, FA_ACT_NONE);
+  if (rc != FA_OK) return rc;
+  rc = fa::check_ln_args(resid, out, M, K, K, K, eps);
+  if (rc != FA_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = fa::launch_gemm(x, w1, hidden, M, N, K, K, N, N, FA_ACT_RELU, s);
+  if (rc != FA_OK) return rc;
+  rc = fa::launch_gemm(hidden, w2, resid, M, K, N, N, K, K, FA_ACT_NONE, s, x, K);
+  if (rc != FA_OK) return rc;
+  return fa::launch_ln(resid, out, M, K, K, K, eps, s);
 }
 
 extern "C" int fa_gemm_act(const void* a, const void* b, void* c, int M, int N, int K,

@@ -10,6 +10,8 @@
 * ``mlp(x, w1, w2)`` -- ``act(x @ w1) @ w2``, the GEMM -> activation -> GEMM of
   ``run_mlp_search.py:58-69`` with the activation fused into GEMM 1.
 * ``gemm_act(a, b, act)`` -- one matmul stage with its fused epilogue.
+* ``mlp_ln(x, w1, w2)`` -- the reference's whole MLP block,
+  ``LayerNorm(relu(x @ w1) @ w2 + x)`` (``run_mlp_search.py:42-127``).
 * ``attention_from_host(...)`` -- the same operator fed from (pinned) host
   tensors: copies in, kernel, copy out, all on the current stream.
 
@@ -221,6 +223,52 @@ def mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, act: str = "gelu_ta
                             out.data_ptr(), M, K, N, _lib.ACTIVATIONS[act],
                             _stream_ptr(x.device))
     _lib.check(rc, "fa_mlp_fwd")
+    return out
+
+
+def mlp_ln(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, eps: float = 1e-5,
+           hidden: torch.Tensor | None = None, resid: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """The reference's MLP block ``LayerNorm(relu(x @ w1) @ w2 + x)`` without
+    affine parameters (``run_mlp_search.py:42-127``, oracle ``:138-149``):
+    ReLU fused into GEMM 1, the residual add into GEMM 2's epilogue, then a
+    row LayerNorm kernel.  ``hidden`` [M, N] and ``resid`` [M, K] are bf16
+    workspaces; K <= 8192."""
+    for name, t in (("x", x), ("w1", w1), ("w2", w2)):
+        _check_cuda_bf16(name, t)
+        if t.dim() != 2 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous 2-D tensor")
+    M, K = x.shape
+    if w1.shape[0] != K or w2.shape[1] != K or w2.shape[0] != w1.shape[1]:
+        raise ValueError(f"bad MLP shapes x{tuple(x.shape)} w1{tuple(w1.shape)} "
+                         f"w2{tuple(w2.shape)}")
+    N = w1.shape[1]
+    hidden = torch.empty((M, N), dtype=_BF16, device=x.device) if hidden is None else hidden
+    resid = torch.empty((M, K), dtype=_BF16, device=x.device) if resid is None else resid
+    out = torch.empty((M, K), dtype=_BF16, device=x.device) if out is None else out
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.fa_mlp_ln_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), hidden.data_ptr(),
+                               resid.data_ptr(), out.data_ptr(), M, K, N, float(eps),
+                               _stream_ptr(x.device))
+    _lib.check(rc, "fa_mlp_ln_fwd")
+    return out
+
+
+def layer_norm_rows(x: torch.Tensor, eps: float = 1e-5,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """``(x - mean) / sqrt(var + eps)`` over the last dimension of a 2-D bf16
+    CUDA tensor (no affine; N a multiple of 8, N <= 8192)."""
+    _check_cuda_bf16("x", x)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be 2-D with a contiguous last dimension")
+    M, N = x.shape
+    out = torch.empty((M, N), dtype=_BF16, device=x.device) if out is None else out
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.fa_layernorm_rows(x.data_ptr(), out.data_ptr(), M, N, x.stride(0),
+                                   out.stride(0), float(eps), _stream_ptr(x.device))
+    _lib.check(rc, "fa_layernorm_rows")
     return out
 
 

@@ -97,6 +97,27 @@ int fa_mlp_fwd(const void* x, const void* w1, const void* w2, void* hidden, void
                int K, int N, int act, void* stream);
 
 /*
+ * The reference's full MLP block (run_mlp_search.py:42-127, checked by its
+ * verify at :138-149):
+ *   hidden = relu(X @ W1)            [M, N]  caller-owned bf16 workspace
+ *   resid  = hidden @ W2 + X         [M, K]  caller-owned bf16 workspace
+ *                                            (residual added in GEMM 2's epilogue)
+ *   out    = (resid - mean) / sqrt(var + eps) over each row (no affine)
+ * K, N multiples of 64; K <= 8192 (the LayerNorm row stays in registers).
+ */
+int fa_mlp_ln_fwd(const void* x, const void* w1, const void* w2, void* hidden, void* resid,
+                  void* out, int M, int K, int N, float eps, void* stream);
+
+/*
+ * Row LayerNorm without affine parameters: out[i, :] = (in[i, :] - mean_i) /
+ * sqrt(var_i + eps), population variance, computed in fp32 (the LayerNorm
+ * stage of run_mlp_search.py:76-93).  N a multiple of 8, N <= 8192; row
+ * strides multiples of 8 elements.
+ */
+int fa_layernorm_rows(const void* in, void* out, int M, int N, int64_t ld_in, int64_t ld_out,
+                      float eps, void* stream);
+
+/*
  * fa_mlp_fwd without any device allocation: the same MLP block, with the
  * hidden activation kept in a fixed array inside the library instead of a
  * caller-provided buffer.  No counterpart in the reference.

@@ -17,7 +17,7 @@ import torch
 from conftest import GOLDEN, assert_close
 import oracle
 from oracle.mlp import round_to_bf16
-from cs348k_fast_attention_grammar_b200 import FaError, gemm_act, mlp
+from cs348k_fast_attention_grammar_b200 import FaError, gemm_act, layer_norm_rows, mlp, mlp_ln
 from cs348k_fast_attention_grammar_b200.inputs import MLP_CONFIGS, make_mlp
 
 pytestmark = pytest.mark.gpu
@@ -93,3 +93,48 @@ def test_gemm_errors():
         gemm_act(a, b)
     with pytest.raises(ValueError):
         gemm_act(a, b, act="tanh")
+
+
+def _ln_np(r, eps=1e-5):
+    r = np.asarray(r, dtype=np.float64)
+    mean = r.mean(axis=1, keepdims=True)
+    var = r.var(axis=1, keepdims=True)
+    return (r - mean) / np.sqrt(var + eps)
+
+
+@pytest.mark.parametrize("M,N", [(64, 64), (257, 512), (100, 4096), (3, 8192), (5, 24)])
+def test_layer_norm_rows_matches_oracle(M, N):
+    x = (_rand((M, N), 9, std=3.0).float() + 1.5).to(torch.bfloat16)
+    out = layer_norm_rows(x.to(DEV))
+    ref = _ln_np(x.float().numpy())
+    assert_close(out.float().cpu().numpy(), ref, what=f"layernorm {M}x{N}")
+
+
+def test_mlp_ln_block_matches_reference_golden():
+    """The reference's whole block LayerNorm(relu(X W1) W2 + X), run by its
+    own emitted program through its numpy stand-in (golden vector).  The kernel
+    stores hidden and the residual sum in bf16, so it is compared with an
+    oracle that rounds those two tensors the same way (standard tolerance) and
+    with the reference's fp32 output (bound covering the two roundings)."""
+    z = np.load(os.path.join(GOLDEN, "mlp_ln_B64_Dm64_H128.npz"))
+    x, w1, w2 = (torch.from_numpy(z[n]).to(torch.bfloat16).to(DEV) for n in ("X", "W1", "W2"))
+    out = mlp_ln(x, w1, w2).float().cpu().numpy()
+    X, W1, W2 = (z[n].astype(np.float64) for n in ("X", "W1", "W2"))
+    h = round_to_bf16(np.maximum(X @ W1, 0)).astype(np.float64)
+    r = round_to_bf16(h @ W2 + X).astype(np.float64)
+    assert_close(out, _ln_np(r), what="mlp_ln vs bf16-storage oracle")
+    assert_close(out, z["O"], max_tol=5e-2, mean_tol=5e-3, what="mlp_ln vs reference program")
+    np.testing.assert_allclose(oracle.mlp_ln_block(z["X"], z["W1"], z["W2"]), z["O"],
+                               rtol=1e-4, atol=1e-4)
+
+
+def test_mlp_ln_block_larger_shape():
+    M, K, N = 384, 512, 1024
+    x = _rand((M, K), 13)
+    w1 = _rand((K, N), 14, std=K ** -0.5)
+    w2 = _rand((N, K), 15, std=N ** -0.5)
+    out = mlp_ln(x.to(DEV), w1.to(DEV), w2.to(DEV)).float().cpu().numpy()
+    X, W1, W2 = (t.double().numpy() for t in (x, w1, w2))
+    h = round_to_bf16(np.maximum(X @ W1, 0)).astype(np.float64)
+    r = round_to_bf16(h @ W2 + X).astype(np.float64)
+    assert_close(out, _ln_np(r), what="mlp_ln 384x512x1024")
