@@ -38,6 +38,28 @@ def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+class _on_device:
+    """Make ``device`` current for the C call (the library launches on the
+    current device); a no-op when it already is, which keeps small calls cheap."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device: torch.device):
+        self.idx = device.index if device.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
 def _check_cuda_bf16(name: str, t: torch.Tensor) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
@@ -76,7 +98,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
         scale = 1.0 / math.sqrt(D)
     lib = _lib.load()
     strides = (ctypes.c_int64 * 16)(*q.stride(), *k.stride(), *v.stride(), *out.stride())
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         rc = lib.fa_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                              B, H, S, D, strides, int(bool(causal)), float(scale),
                              _stream_ptr(q.device))
@@ -188,7 +210,7 @@ def gemm_act(a: torch.Tensor, b: torch.Tensor, act: str = "none",
     if out is None:
         out = torch.empty((M, N), dtype=_BF16, device=a.device)
     lib = _lib.load()
-    with torch.cuda.device(a.device):
+    with _on_device(a.device):
         rc = lib.fa_gemm_act(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
                              a.stride(0), b.stride(0), out.stride(0),
                              _lib.ACTIVATIONS[act], _stream_ptr(a.device))
@@ -218,7 +240,7 @@ def mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, act: str = "gelu_ta
     if out is None:
         out = torch.empty((M, K), dtype=_BF16, device=x.device)
     lib = _lib.load()
-    with torch.cuda.device(x.device):
+    with _on_device(x.device):
         rc = lib.fa_mlp_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), hidden.data_ptr(),
                             out.data_ptr(), M, K, N, _lib.ACTIVATIONS[act],
                             _stream_ptr(x.device))
@@ -247,7 +269,7 @@ def mlp_ln(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, eps: float = 1e-
     resid = torch.empty((M, K), dtype=_BF16, device=x.device) if resid is None else resid
     out = torch.empty((M, K), dtype=_BF16, device=x.device) if out is None else out
     lib = _lib.load()
-    with torch.cuda.device(x.device):
+    with _on_device(x.device):
         rc = lib.fa_mlp_ln_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), hidden.data_ptr(),
                                resid.data_ptr(), out.data_ptr(), M, K, N, float(eps),
                                _stream_ptr(x.device))
@@ -265,7 +287,7 @@ def layer_norm_rows(x: torch.Tensor, eps: float = 1e-5,
     M, N = x.shape
     out = torch.empty((M, N), dtype=_BF16, device=x.device) if out is None else out
     lib = _lib.load()
-    with torch.cuda.device(x.device):
+    with _on_device(x.device):
         rc = lib.fa_layernorm_rows(x.data_ptr(), out.data_ptr(), M, N, x.stride(0),
                                    out.stride(0), float(eps), _stream_ptr(x.device))
     _lib.check(rc, "fa_layernorm_rows")
