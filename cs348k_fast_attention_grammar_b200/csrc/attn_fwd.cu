@@ -111,7 +111,10 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 template <int D>
 struct AttnCfg {
   static constexpr int kTileBytes = kBM * D * 2;          // one 128 x D bf16 tile
-  static constexpr int kStages = (D == 128) ? 4 : 8;      // K/V ring slots
+#ifndef FA_ATTN_STAGES_D128
+#define FA_ATTN_STAGES_D128 4
+#endif
+  static constexpr int kStages = (D == 128) ? FA_ATTN_STAGES_D128 : 8;   // K/V ring slots
   static constexpr int kQOff = 0;
   static constexpr int kKVOff = 2 * kTileBytes;
   static constexpr int kBarOff = kKVOff + kStages * kTileBytes;
