@@ -55,6 +55,14 @@ constexpr float kRescaleThreshold = 8.0f;
 #endif
 // 1 = P is published in two halves (keys 0-63, 64-127) so the first half of
 // O += P V starts while the softmax computes the second half.
+// Upper bound on the K/V bytes of one scheduling group of (batch, head) pairs.
+// ncu on this pool: groups of 64 MiB re-read K/V from DRAM (cfg2 small case
+// 270 MB read for 201 MB of Q/K/V, D = 64 case 2.2x), groups of <= 32 MiB do
+// not (the L2 is split over the two dies, so half of it is what one working
+// set can count on).
+#ifndef FA_ATTN_GROUP_MIB
+#define FA_ATTN_GROUP_MIB 32
+#endif
 #ifndef FA_ATTN_SPLIT_P
 #define FA_ATTN_SPLIT_P 1
 #endif
@@ -131,7 +139,8 @@ struct AttnCfg {
 struct AttnParams {
   int B, H, S;
   int n_units_per_head;   // ceil(S / 256)
-  int group_heads;        // (batch, head) pairs per scheduling group
+  int group_q;            // scheduling groups hold group_q or group_q + 1 pairs;
+  int group_r;            // the first group_r groups hold group_q + 1
   int nkv;                // ceil(S / 128)
   float scale_log2;       // scale * log2(e)
   __nv_bfloat16* o;
@@ -200,16 +209,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
 
   // ---- work unit ------------------------------------------------------------
-  // (batch, head) pairs are taken in groups of p.group_heads (K/V of a group
-  // stay resident in L2).  Inside a group the units run query-position-major,
-  // and for causal attention the longest (last) query units of every head of
-  // the group go first, so the short units fill the tail.
-  const int group_units = p.group_heads * p.n_units_per_head;
-  const int grp = blockIdx.x / group_units;
-  const int r_in = blockIdx.x - grp * group_units;
-  const int heads_here = min(p.group_heads, p.B * p.H - grp * p.group_heads);
+  // (batch, head) pairs are taken in consecutive groups of group_q + 1 (the
+  // first group_r groups) or group_q pairs, so the K/V of a group stay
+  // resident in L2.  Inside a group the units run query-position-major, and
+  // for causal attention the longest (last) query units of every head of the
+  // group go first, so the short units fill the tail.
+  int heads_here, first_bh, r_in;
+  {
+    const int big_units = (p.group_q + 1) * p.n_units_per_head;
+    const int big_span = p.group_r * big_units;
+    if (static_cast<int>(blockIdx.x) < big_span) {
+      const int g = blockIdx.x / big_units;
+      r_in = blockIdx.x - g * big_units;
+      heads_here = p.group_q + 1;
+      first_bh = g * heads_here;
+    } else {
+      const int x = blockIdx.x - big_span;
+      const int small_units = p.group_q * p.n_units_per_head;
+      const int g = x / small_units;
+      r_in = x - g * small_units;
+      heads_here = p.group_q;
+      first_bh = p.group_r * (p.group_q + 1) + g * p.group_q;
+    }
+  }
   int qu = r_in / heads_here;
-  const int bh = grp * p.group_heads + (r_in - qu * heads_here);
+  const int bh = first_bh + (r_in - qu * heads_here);
   if (CAUSAL) qu = p.n_units_per_head - 1 - qu;
   const int b = bh / p.H;
   const int h = bh - b * p.H;
@@ -608,13 +632,19 @@ extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o,
   prm.H = H;
   prm.S = S;
   prm.n_units_per_head = (S + 2 * kBM - 1) / (2 * kBM);
-  // Group size: about 64 MiB of K/V per group (half the 126 MB L2), >= 1.
+  // Groups: at most FA_ATTN_GROUP_MIB of K/V each (>= 1 pair), the pairs
+  // split as evenly as possible over them, since a short last group starts its
+  // longest units late and leaves a tail.
   {
+    const int64_t pairs = static_cast<int64_t>(B) * H;
     const int64_t kv_bytes_per_head = 2ll * S * D * 2;
-    int64_t g = (64ll << 20) / (kv_bytes_per_head > 0 ? kv_bytes_per_head : 1);
+    int64_t g = (static_cast<int64_t>(FA_ATTN_GROUP_MIB) << 20) /
+                (kv_bytes_per_head > 0 ? kv_bytes_per_head : 1);
     if (g < 1) g = 1;
-    if (g > static_cast<int64_t>(B) * H) g = static_cast<int64_t>(B) * H;
-    prm.group_heads = static_cast<int>(g);
+    if (g > pairs) g = pairs;
+    const int64_t n_groups = (pairs + g - 1) / g;
+    prm.group_q = static_cast<int>(pairs / n_groups);
+    prm.group_r = static_cast<int>(pairs % n_groups);
   }
   prm.nkv = (S + kBN - 1) / kBN;
   prm.scale_log2 = scale * 1.4426950408889634f;
