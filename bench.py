@@ -479,6 +479,14 @@ def bench_ref512(args, fab, device, world, rank):
     with ClockSampler(local_index(device)) as clk:
         ms = timed_loop(step, args.steps, world, device)
     value = REF512_FLOPS * world / (ms * 1e-3) / 1e12
+    # Like-for-like on the same GPU: the reference's flash-attn2-sota.py call,
+    # torch SDPA on [1, 1, 512, 64] fp32 (its fn(K, Q, V)), timed the same way.
+    KT, Q, V = ins
+    k4, q4, v4 = (t.reshape(1, 1, 512, 64) for t in (KT.t().contiguous(), Q, V))
+    sdpa = lambda: torch.nn.functional.scaled_dot_product_attention(q4, k4, v4)  # noqa: E731
+    for _ in range(max(args.warmup, 0)):
+        sdpa()
+    ms_sdpa = timed_loop(sdpa, args.steps, world, device)
     peaks = load_peaks()
     return {"metric": "reference kernel-module attention TFLOP/s (program_flops, N=512 d=64)",
             "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
@@ -491,7 +499,11 @@ def bench_ref512(args, fab, device, world, rank):
                                    "non-causal, kernel-module protocol",
                        "l2": "not flushed (1 MB of inputs)"},
             "roofline": roofline(4 * 512 * 512 * 64 / (ms * 1e-3) / 1e12, peaks, None),
-            "gpu_launches": args.steps, "clocks": clk.summary(), "cpu_baseline": None,
+            "sdpa_same_gpu": {"value": REF512_FLOPS * world / (ms_sdpa * 1e-3) / 1e12,
+                              "unit": "TFLOP/s", "ms_per_call": ms_sdpa,
+                              "what": "torch scaled_dot_product_attention fp32 [1,1,512,64] "
+                                      "(flash-attn2-sota.py's call) on this GPU"},
+            "gpu_launches": 2 * args.steps, "clocks": clk.summary(), "cpu_baseline": None,
             "e2e": None}
 
 

@@ -143,7 +143,7 @@ struct AttnParams {
   int group_r;            // the first group_r groups hold group_q + 1
   int nkv;                // ceil(S / 128)
   float scale_log2;       // scale * log2(e)
-  __nv_bfloat16* o;
+  void* o;               // bf16, or fp32 when OUT_F32
   int64_t o_sb, o_sh, o_ss;
   int* status;
   unsigned long long* trace;   // timeline buffer (trace builds only), else null
@@ -176,7 +176,7 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, bool OUT_F32>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
@@ -535,23 +535,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && nt[t] > 0 && mbar_wait(bar_o_full(t), 0, abort_flag, p.status)) {
       tc_fence_after();
       const float inv_l = 1.f / l;
-      __nv_bfloat16* orow = p.o + static_cast<int64_t>(b) * p.o_sb +
-                            static_cast<int64_t>(h) * p.o_sh + static_cast<int64_t>(qi) * p.o_ss;
+      const int64_t orow_off = static_cast<int64_t>(b) * p.o_sb +
+                               static_cast<int64_t>(h) * p.o_sh + static_cast<int64_t>(qi) * p.o_ss;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         tmem_ld32_wait(tO + c * 32, o);
-        uint32_t w[16];
+        if (OUT_F32) {
+          // fp32 output (the reference's own dtype): 8 x 16-byte stores.
+          if (qi < p.S) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<float*>(p.o) + orow_off + c * 32);
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          w[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv_l,
-                             __uint_as_float(o[2 * e + 1]) * inv_l);
-        if (qi < p.S) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-          dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
-          dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+            for (int e = 0; e < 8; ++e)
+              dst[e] = make_uint4(__float_as_uint(__uint_as_float(o[4 * e]) * inv_l),
+                                  __float_as_uint(__uint_as_float(o[4 * e + 1]) * inv_l),
+                                  __float_as_uint(__uint_as_float(o[4 * e + 2]) * inv_l),
+                                  __float_as_uint(__uint_as_float(o[4 * e + 3]) * inv_l));
+          }
+        } else {
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            w[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv_l,
+                               __uint_as_float(o[2 * e + 1]) * inv_l);
+          if (qi < p.S) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + orow_off +
+                                                  c * 32);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+            dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+          }
         }
       }
     }
@@ -566,11 +580,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, bool OUT_F32>
 int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                 const AttnParams& prm, int grid, cudaStream_t stream) {
   using C = AttnCfg<D>;
-  auto kern = attn_fwd_kernel<D, CAUSAL>;
+  auto kern = attn_fwd_kernel<D, CAUSAL, OUT_F32>;
   static bool attr_set[64] = {};
   int dev = 0;
   int rc = FA_OK;
@@ -601,24 +615,13 @@ extern "C" void fa_attn_set_trace_buffer(void* buf) {
 }
 #endif
 
-extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int H,
-                           int S, int D, const int64_t* st, int causal, float scale,
-                           void* stream) {
-  using namespace fa;
-  if (!q || !k || !v || !o || !st) return FA_ERR_NULL;
-  if (B <= 0 || H <= 0 || S <= 0) return FA_ERR_SHAPE;
-  if (D != 64 && D != 128) return FA_ERR_HEAD_DIM;
-  const int64_t units = static_cast<int64_t>(B) * H * ((S + 2 * kBM - 1) / (2 * kBM));
-  if (units > 0x7fffffffLL) return FA_ERR_SHAPE;
-  for (int t = 0; t < 4; ++t) {
-    if (st[4 * t + 3] != 1) return FA_ERR_STRIDE;
-    for (int i = 0; i < 3; ++i)
-      if (st[4 * t + i] <= 0 || (st[4 * t + i] % 8) != 0) return FA_ERR_ALIGN;
-  }
-  const void* ptrs[4] = {q, k, v, o};
-  for (int t = 0; t < 4; ++t)
-    if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 != 0) return FA_ERR_ALIGN;
+namespace fa {
+namespace {
 
+// Shared host path of fa_attn_fwd / fa_attn_fwd_f32 (arguments already
+// validated): tensor maps, scheduling groups, launch.
+int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D,
+             const int64_t* st, int causal, float scale, bool out_f32, cudaStream_t stream) {
   int dev = 0;
   int rc = prepare_device(nullptr, 0, &dev);
   if (rc != FA_OK) return rc;
@@ -648,18 +651,114 @@ extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o,
   }
   prm.nkv = (S + kBN - 1) / kBN;
   prm.scale_log2 = scale * 1.4426950408889634f;
-  prm.o = static_cast<__nv_bfloat16*>(o);
+  prm.o = o;
   prm.o_sb = st[12];
   prm.o_sh = st[13];
   prm.o_ss = st[14];
   prm.status = device_status_ptr();
   prm.trace = g_trace_buffer;
   if (prm.status == nullptr) return FA_ERR_CUDA;
-  const int grid = static_cast<int>(units);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = static_cast<int>(static_cast<int64_t>(B) * H * prm.n_units_per_head);
+  if (out_f32) {
+    if (D == 64)
+      return causal ? launch_attn<64, true, true>(mq, mk, mv, prm, grid, stream)
+                    : launch_attn<64, false, true>(mq, mk, mv, prm, grid, stream);
+    return causal ? launch_attn<128, true, true>(mq, mk, mv, prm, grid, stream)
+                  : launch_attn<128, false, true>(mq, mk, mv, prm, grid, stream);
+  }
   if (D == 64)
-    return causal ? launch_attn<64, true>(mq, mk, mv, prm, grid, s)
-                  : launch_attn<64, false>(mq, mk, mv, prm, grid, s);
-  return causal ? launch_attn<128, true>(mq, mk, mv, prm, grid, s)
-                : launch_attn<128, false>(mq, mk, mv, prm, grid, s);
+    return causal ? launch_attn<64, true, false>(mq, mk, mv, prm, grid, stream)
+                  : launch_attn<64, false, false>(mq, mk, mv, prm, grid, stream);
+  return causal ? launch_attn<128, true, false>(mq, mk, mv, prm, grid, stream)
+                : launch_attn<128, false, false>(mq, mk, mv, prm, grid, stream);
+}
+
+// fp32 -> bf16 staging of the reference's 2-D operands into the workspace
+// [q | k | v], each [N, D] row-major.  blockIdx.z picks the tensor; K comes
+// either as [N, D] or transposed as KT [D, N] (then a 32 x 32 tile goes
+// through shared memory so reads and writes both stay coalesced).
+__global__ void __launch_bounds__(256)
+    stage_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                     const float* __restrict__ v, __nv_bfloat16* __restrict__ ws, int N, int D,
+                     int k_transposed) {
+  __shared__ float tile[32][33];
+  const int z = blockIdx.z;
+  const float* src = (z == 0) ? q : (z == 1) ? k : v;
+  __nv_bfloat16* dst = ws + static_cast<int64_t>(z) * N * D;
+  const int n0 = blockIdx.x * 32;
+  const int d0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31;
+  const int ty = threadIdx.x >> 5;   // 0..7
+  if (z == 1 && k_transposed) {
+#pragma unroll
+    for (int r = ty; r < 32; r += 8) {      // r = d within the tile, read along n
+      const int d = d0 + r, n = n0 + tx;
+      tile[r][tx] = (n < N) ? src[static_cast<int64_t>(d) * N + n] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = ty; r < 32; r += 8) {      // r = n within the tile, write along d
+      const int n = n0 + r;
+      if (n < N) dst[static_cast<int64_t>(n) * D + d0 + tx] = __float2bfloat16_rn(tile[tx][r]);
+    }
+  } else {
+#pragma unroll
+    for (int r = ty; r < 32; r += 8) {
+      const int n = n0 + r;
+      if (n < N) {
+        const int64_t i = static_cast<int64_t>(n) * D + d0 + tx;
+        dst[i] = __float2bfloat16_rn(src[i]);
+      }
+    }
+  }
+}
+
+}  // namespace
+}  // namespace fa
+
+extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int H,
+                           int S, int D, const int64_t* st, int causal, float scale,
+                           void* stream) {
+  using namespace fa;
+  if (!q || !k || !v || !o || !st) return FA_ERR_NULL;
+  if (B <= 0 || H <= 0 || S <= 0) return FA_ERR_SHAPE;
+  if (D != 64 && D != 128) return FA_ERR_HEAD_DIM;
+  const int64_t units = static_cast<int64_t>(B) * H * ((S + 2 * kBM - 1) / (2 * kBM));
+  if (units > 0x7fffffffLL) return FA_ERR_SHAPE;
+  for (int t = 0; t < 4; ++t) {
+    if (st[4 * t + 3] != 1) return FA_ERR_STRIDE;
+    for (int i = 0; i < 3; ++i)
+      if (st[4 * t + i] <= 0 || (st[4 * t + i] % 8) != 0) return FA_ERR_ALIGN;
+  }
+  const void* ptrs[4] = {q, k, v, o};
+  for (int t = 0; t < 4; ++t)
+    if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 != 0) return FA_ERR_ALIGN;
+  return run_attn(q, k, v, o, B, H, S, D, st, causal, scale, false,
+                  static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fa_attn_fwd_f32(const void* q, const void* k, const void* v, void* o, void* ws,
+                               int N, int D, int k_transposed, int causal, float scale,
+                               void* stream) {
+  using namespace fa;
+  if (!q || !k || !v || !o || !ws) return FA_ERR_NULL;
+  if (N <= 0 || (k_transposed != 0 && k_transposed != 1)) return FA_ERR_SHAPE;
+  if (D != 64 && D != 128) return FA_ERR_HEAD_DIM;
+  if (static_cast<int64_t>(N) * D > (1ll << 28)) return FA_ERR_SHAPE;
+  const void* ptrs[5] = {q, k, v, o, ws};
+  for (int t = 0; t < 5; ++t)
+    if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 != 0) return FA_ERR_ALIGN;
+  int dev = 0;
+  int rc = prepare_device(nullptr, 0, &dev);
+  if (rc != FA_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  __nv_bfloat16* wb = static_cast<__nv_bfloat16*>(ws);
+  const dim3 grid((N + 31) / 32, D / 32, 3);
+  stage_f32_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(q),
+                                       static_cast<const float*>(k),
+                                       static_cast<const float*>(v), wb, N, D, k_transposed);
+  if (cudaGetLastError() != cudaSuccess) return FA_ERR_LAUNCH;
+  const int64_t nd = static_cast<int64_t>(N) * D;
+  const int64_t st[16] = {nd, nd, D, 1, nd, nd, D, 1, nd, nd, D, 1, nd, nd, D, 1};
+  return run_attn(wb, wb + nd, wb + 2 * nd, o, 1, 1, N, D, st, causal, scale, true, s);
 }

@@ -4,6 +4,8 @@
   the operator behind the reference's kernel-module protocol (``bench.py:14-20``;
   ``pytorch-naive.py:23-65``, ``flash-attn2-sota.py:41-63``,
   ``old/kernels/old/naive.py:27-56``).
+* ``attention_f32(q, k, v, k_transposed=False)`` -- the reference's own 2-D
+  fp32 problem (``fn(KT, Q, V)``), staged to bf16 on the device in one call.
 * ``attention_bshd(q, k, v, causal=False)`` -- the legacy ``(B, S, H, D)``
   layout of ``old/benchmark.py:17-21``, passed to the kernel as strides (no
   permute copy).
@@ -103,6 +105,44 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
                              B, H, S, D, strides, int(bool(causal)), float(scale),
                              _stream_ptr(q.device))
     _lib.check(rc, "fa_attn_fwd")
+    return out
+
+
+def attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+                  scale: float | None = None, k_transposed: bool = False,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """The reference's own 2-D fp32 problem: ``q [N, D]``, ``k [N, D]`` (or
+    ``KT [D, N]`` with ``k_transposed=True``), ``v [N, D]`` contiguous fp32
+    CUDA tensors -> ``o [N, D]`` fp32.  One C call: the operands are staged to
+    bf16 on the device and the attention epilogue writes fp32 (the
+    ``fn(KT, Q, V)`` of ``pytorch-naive.py:23`` and the emitted modules)."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor (got device {t.device})")
+        if t.dtype != torch.float32:
+            raise TypeError(f"{name} must be float32 (got {t.dtype})")
+        if t.dim() != 2 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous 2-D tensor")
+    N, D = q.shape
+    kshape = (D, N) if k_transposed else (N, D)
+    if tuple(v.shape) != (N, D) or tuple(k.shape) != kshape:
+        raise ValueError(f"shapes q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} "
+                         f"do not match (k expected {kshape})")
+    if not (q.device == k.device == v.device):
+        raise ValueError("q, k, v must be on the same device")
+    if out is None:
+        out = torch.empty((N, D), dtype=torch.float32, device=q.device)
+    ws = torch.empty(3 * N * D, dtype=_BF16, device=q.device)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    lib = _lib.load()
+    with _on_device(q.device):
+        rc = lib.fa_attn_fwd_f32(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                 ws.data_ptr(), N, D, int(bool(k_transposed)),
+                                 int(bool(causal)), float(scale), _stream_ptr(q.device))
+    _lib.check(rc, "fa_attn_fwd_f32")
     return out
 
 

@@ -16,6 +16,9 @@
  *                   modules pytorch-naive.py:23-65 and flash-attn2-sota.py:41-63,
  *                   and the batched attention(q, k, v) of
  *                   old/kernels/old/naive.py:27-56 / old/benchmark.py:17-21.
+ *   fa_attn_fwd_f32 <- the same callables at the reference's own fp32 2-D
+ *                   problem (fn(KT, Q, V) with fp32 cupy arrays), staging to
+ *                   bf16 on the device instead of host-side casts.
  *   fa_mlp_fwd   <- the host callable emitted for the MLP program of
  *                   run_mlp_search.py:42-127 (stages h = X@W1, a = act(h),
  *                   y = a@W2 at :58-69).
@@ -76,6 +79,22 @@ int fa_version(void);
  */
 int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int H, int S,
                 int D, const int64_t* strides, int causal, float scale, void* stream);
+
+/*
+ * The reference's own 2-D fp32 problem in one call (the kernel-module
+ * callables fn(KT, Q, V) of pytorch-naive.py:23 and of every emitted module,
+ * grammar/kernel_ast.py:1267-1287, and fn(K, Q, V) of flash-attn2-sota.py:41
+ * on one (batch, head) pair):
+ *   q [N, D], v [N, D], o [N, D] fp32, contiguous;
+ *   k [N, D] fp32 (k_transposed = 0) or KT [D, N] fp32 (k_transposed = 1);
+ *   ws         : bf16 workspace of 3 * N * D elements (16-byte aligned), where
+ *                q, k, v are staged in bf16 (one launch) for the tensor cores;
+ *   D          : 64 or 128; causal, scale, stream as for fa_attn_fwd.
+ * Two launches (staging, attention); O is written in fp32 by the attention
+ * epilogue.  Inputs are rounded to bf16, accumulation is fp32.
+ */
+int fa_attn_fwd_f32(const void* q, const void* k, const void* v, void* o, void* ws, int N,
+                    int D, int k_transposed, int causal, float scale, void* stream);
 
 /*
  * C[M, N] = act(A[M, K] @ B[K, N]) in bf16 with fp32 accumulation.

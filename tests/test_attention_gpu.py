@@ -15,7 +15,8 @@ import torch
 from conftest import GOLDEN, assert_close
 import oracle
 from cs348k_fast_attention_grammar_b200 import (FaError, attention, attention_bshd,
-                                                attention_from_host, device_status)
+                                                attention_f32, attention_from_host,
+                                                device_status)
 from cs348k_fast_attention_grammar_b200 import kernel_module
 from cs348k_fast_attention_grammar_b200.inputs import ATTN_CONFIGS, make_qkv
 
@@ -57,6 +58,40 @@ def test_attention_matches_reference_program(name):
                            torch.from_numpy(z["V"]).to(DEV))
     torch.cuda.synchronize()
     assert_close(out.cpu().numpy(), z["O"], what=name)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("N", [512, 200, 1000, 1])
+@pytest.mark.parametrize("k_transposed", [True, False])
+def test_attention_f32_matches_oracle(N, D, causal, k_transposed):
+    """The fp32 2-D entry point (device-side bf16 staging, fp32 output):
+    against the oracle on the bf16-rounded inputs (standard tolerance) and on
+    the fp32 inputs themselves (looser bound covering the input rounding)."""
+    g = torch.Generator().manual_seed(N * 7 + D + int(causal))
+    q, k, v = (torch.randn((N, D), generator=g) for _ in range(3))
+    kin = k.t().contiguous() if k_transposed else k
+    out = attention_f32(q.to(DEV), kin.to(DEV), v.to(DEV), causal=causal,
+                        k_transposed=k_transposed)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float32 and tuple(out.shape) == (N, D)
+    r = lambda t: t.to(torch.bfloat16).float().numpy()[None, None]  # noqa: E731
+    ref = oracle.attention(r(q), r(k), r(v), causal=causal)[0, 0]
+    assert_close(out.cpu().numpy(), ref, what=f"f32 N{N} D{D} causal={causal}")
+    ref32 = oracle.attention(q.numpy()[None, None], k.numpy()[None, None], v.numpy()[None, None],
+                             causal=causal)[0, 0]
+    assert_close(out.cpu().numpy(), ref32, max_tol=5e-2, mean_tol=5e-3, what="f32 vs fp32 inputs")
+
+
+def test_attention_f32_errors():
+    q = torch.randn(512, 64, device=DEV)
+    with pytest.raises(TypeError):
+        attention_f32(q.half(), q.half(), q.half())
+    with pytest.raises(ValueError):
+        attention_f32(q, q[:256], q)
+    with pytest.raises(FaError, match="head dimension"):
+        x = torch.randn(512, 32, device=DEV)
+        attention_f32(x, x, x)
 
 
 def test_attention_matches_sota_module():

@@ -72,6 +72,12 @@ def test_argument_checks_without_device():
     odd = ctypes.c_void_p(258)
     assert lib.fa_attn_fwd(odd, p, p, p, 1, 1, 16, 64, st, 0, 0.125, None) == \
         codes["FA_ERR_ALIGN"]
+    f32 = lib.fa_attn_fwd_f32
+    assert f32(p, p, p, p, None, 512, 64, 1, 0, 0.125, None) == codes["FA_ERR_NULL"]
+    assert f32(p, p, p, p, p, 0, 64, 1, 0, 0.125, None) == codes["FA_ERR_SHAPE"]
+    assert f32(p, p, p, p, p, 512, 64, 2, 0, 0.125, None) == codes["FA_ERR_SHAPE"]
+    assert f32(p, p, p, p, p, 512, 32, 1, 0, 0.125, None) == codes["FA_ERR_HEAD_DIM"]
+    assert f32(p, p, p, p, odd, 512, 64, 1, 0, 0.125, None) == codes["FA_ERR_ALIGN"]
     assert lib.fa_gemm_act(p, p, p, 128, 100, 64, 64, 100, 100, 0, None) == codes["FA_ERR_SHAPE"]
     assert lib.fa_gemm_act(p, p, p, 128, 128, 64, 64, 128, 128, 7, None) == codes["FA_ERR_ARG"]
     assert lib.fa_gemm_act(p, p, p, 128, 128, 64, 60, 128, 128, 0, None) == \
