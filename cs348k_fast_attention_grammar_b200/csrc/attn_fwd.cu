@@ -419,12 +419,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY;   // reference row max, already scaled (log2 domain)
     float l = 0.f;             // running row sum of exp2(s * sl2 - m_ref)
     bool ok = true;
+    // Warp-uniform bounded wait: every lane waits, and the warp goes on only
+    // if all lanes saw the phase complete, so an abort never splits a warp
+    // ahead of the warp-wide votes and TMEM accesses below.
+    auto wwait = [&](uint32_t bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status));
+    };
     const int q_tile0 = q0 + t * kBM;
     constexpr bool kPingPong = (D == 64) ? (FA_ATTN_PINGPONG_D64 != 0) : (FA_ATTN_PINGPONG_D128 != 0);
     const bool pingpong = kPingPong && nt[0] > 0 && nt[1] > 0;
     for (int j = 0; j < nt[t]; ++j) {
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 0);
-      if (!mbar_wait(bar_s_full(t), j & 1, abort_flag, p.status)) {
+      if (!wwait(bar_s_full(t), j & 1)) {
         ok = false;
         break;
       }
@@ -484,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // works on the other tile.  Tile 0's turn j follows tile 1's turn j-1;
       // tile 1's turn j follows tile 0's turn j.
       if (pingpong && (t == 1 || j > 0) &&
-          !mbar_wait(bar_turn(t), t == 0 ? ((j - 1) & 1) : (j & 1), abort_flag, p.status)) {
+          !wwait(bar_turn(t), t == 0 ? ((j - 1) & 1) : (j & 1))) {
         ok = false;
         break;
       }
@@ -527,12 +533,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Causal units give tile 0 one block fewer than tile 1: pass the turn for
     // tile 1's last block without work.
     if (ok && pingpong && t == 0 && nt[0] < nt[1]) {
-      if (mbar_wait(bar_turn(0), (nt[0] - 1) & 1, abort_flag, p.status))
+      if (wwait(bar_turn(0), (nt[0] - 1) & 1))
         mbar_arrive(bar_turn(1));
       else
         ok = false;
     }
-    if (ok && nt[t] > 0 && mbar_wait(bar_o_full(t), 0, abort_flag, p.status)) {
+    if (ok && nt[t] > 0 && wwait(bar_o_full(t), 0)) {
       tc_fence_after();
       const float inv_l = 1.f / l;
       const int64_t orow_off = static_cast<int64_t>(b) * p.o_sb +

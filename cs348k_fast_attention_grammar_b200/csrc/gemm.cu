@@ -201,7 +201,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
       tile_coords(p, tile, tm, tn);
       const int acc = tcount & 1;
       const uint32_t use = static_cast<uint32_t>(tcount >> 1);
-      if (!mbar_wait(bar_acc_full(acc), use & 1u, abort_flag, p.status)) break;
+      // Warp-uniform: the TMEM loads below are warp-collective, so a wait
+      // that gave up on some lanes ends the loop for the whole warp.
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_acc_full(acc), use & 1u, abort_flag, p.status)))
+        break;
       tc_fence_after();
       const int row = tm * kGBM + row_in_tile;
       __nv_bfloat16* crow = p.c + static_cast<int64_t>(row) * p.ldc + tn * kGBN;
