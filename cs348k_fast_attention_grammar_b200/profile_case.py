@@ -2,10 +2,12 @@
 
     python -m cs348k_fast_attention_grammar_b200.profile_case --config cfg2 --pairs 32
     python -m cs348k_fast_attention_grammar_b200.profile_case --config cfg3 --rows 2048
+    python -m cs348k_fast_attention_grammar_b200.profile_case --config ln --rows 16384
 
 Attention: the first ``--pairs`` (batch, head) pairs of a BASELINE config at
 its full S and D (the same kernel, fewer pairs per launch); MLP: the first
-``--rows`` rows of X with the config's full weights.  Inputs are generated
+``--rows`` rows of X with the config's full weights; ``ln``: the row
+LayerNorm on ``--rows`` rows of cfg3's feature width (4096).  Inputs are generated
 before the launches; ``--iters`` launches follow (so ``ncu -s 1 -c 1`` skips
 a cold first launch).  Prints the CUDA-event time per launch.
 """
@@ -17,13 +19,13 @@ import argparse
 import torch
 
 from .inputs import ATTN_CONFIGS, MLP_CONFIGS, make_mlp, make_qkv
-from .operators import attention, gemm_act
+from .operators import attention, gemm_act, layer_norm_rows
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", default="cfg2",
-                    choices=sorted(list(ATTN_CONFIGS) + list(MLP_CONFIGS)))
+                    choices=sorted(list(ATTN_CONFIGS) + list(MLP_CONFIGS) + ["ln"]))
     ap.add_argument("--pairs", type=int, default=32)
     ap.add_argument("--rows", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=3)
@@ -40,6 +42,17 @@ def main(argv=None):
             attention(q, k, v, causal=cfg["causal"], out=o)
         ev[1].record()
         what = f"attention {a.config} pairs={a.pairs} S={cfg['S']} D={cfg['D']}"
+    elif a.config == "ln":
+        K = MLP_CONFIGS["cfg3"]["K"]
+        g = torch.Generator(device=dev).manual_seed(0)
+        x = torch.randn((a.rows, K), generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        torch.cuda.synchronize()
+        ev[0].record()
+        for _ in range(a.iters):
+            layer_norm_rows(x, out=y)
+        ev[1].record()
+        what = f"layer_norm rows={a.rows} N={K}"
     else:
         cfg = dict(MLP_CONFIGS[a.config], M=a.rows)
         x, w1, w2 = make_mlp(cfg, dev)
