@@ -7,8 +7,9 @@
 // chip (tensor memory) and streams K/V once per CTA.
 //
 // Work unit (one CTA): one (batch, head) pair and 256 query rows, held as two
-// 128-row Q tiles that ping-pong between the tensor cores and the softmax
-// warps.  Warp roles (12 warps, 384 threads):
+// 128-row Q tiles that alternate between the tensor cores and the softmax
+// warps (while one tile's softmax runs, the tensor core works on the other
+// tile's GEMMs).  Warp roles (12 warps, 384 threads):
 //   warps 0-3  softmax for Q tile 0 (thread = one query row = one TMEM lane)
 //   warps 4-7  softmax for Q tile 1
 //   warp  8    TMA producer: Q tiles once, then K_j / V_j 128-key blocks into
@@ -22,7 +23,13 @@
 // Per KV block j the MMA warp issues, in this order,
 //   O_0 += P_0(j-1) V_{j-1};  S_0 = Q_0 K_j^T;  O_1 += P_1(j-1) V_{j-1};  S_1 = Q_1 K_j^T
 // so "S_t(j) complete" implies "O_t holds all blocks < j", which is when the
-// softmax warps may rescale O_t in place.
+// softmax warps may rescale O_t in place.  P is published in two halves (keys
+// 0-63, then 64-127), and O_t += P_t V starts on the first half while the
+// softmax computes the second.  At D = 64 the two softmax warpgroups also take
+// turns on their exponential phases; 25 % of those exponentials run on the
+// FMA pipe.
+// Scheduling: (batch, head) pairs in groups of <= 32 MiB of K/V (L2-resident),
+// causal units longest first within a group.
 // Online softmax (exp2 domain, log2(e) folded into the scale): the running
 // row maximum is only raised when a block's maximum exceeds it by more than
 // 8 (a factor 256), which keeps O_t rescales rare; the final O / l is exact
@@ -53,8 +60,6 @@ constexpr float kRescaleThreshold = 8.0f;
 #ifndef FA_ATTN_PACK_ALU
 #define FA_ATTN_PACK_ALU 0
 #endif
-// 1 = P is published in two halves (keys 0-63, 64-127) so the first half of
-// O += P V starts while the softmax computes the second half.
 // Upper bound on the K/V bytes of one scheduling group of (batch, head) pairs.
 // ncu on this pool: groups of 64 MiB re-read K/V from DRAM (cfg2 small case
 // 270 MB read for 201 MB of Q/K/V, D = 64 case 2.2x), groups of <= 32 MiB do
@@ -63,6 +68,8 @@ constexpr float kRescaleThreshold = 8.0f;
 #ifndef FA_ATTN_GROUP_MIB
 #define FA_ATTN_GROUP_MIB 32
 #endif
+// 1 = P is published in two halves (keys 0-63, 64-127) so the first half of
+// O += P V starts while the softmax computes the second half.
 #ifndef FA_ATTN_SPLIT_P
 #define FA_ATTN_SPLIT_P 1
 #endif
