@@ -25,9 +25,10 @@ from .operators import (  # noqa: F401
     gemm_act,
     layer_norm_rows,
     mlp,
+    mlp_from_host,
     mlp_ln,
 )
 
-__all__ = ["attention", "attention_bshd", "attention_f32", "attention_from_host", "mlp", "mlp_ln",
+__all__ = ["attention", "attention_bshd", "attention_f32", "attention_from_host", "mlp", "mlp_from_host", "mlp_ln",
            "layer_norm_rows", "gemm_act",
            "device_status", "FaError", "load", "lib_path"]

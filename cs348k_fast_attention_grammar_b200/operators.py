@@ -14,8 +14,9 @@
 * ``gemm_act(a, b, act)`` -- one matmul stage with its fused epilogue.
 * ``mlp_ln(x, w1, w2)`` -- the reference's whole MLP block,
   ``LayerNorm(relu(x @ w1) @ w2 + x)`` (``run_mlp_search.py:42-127``).
-* ``attention_from_host(...)`` -- the same operator fed from (pinned) host
-  tensors: copies in, kernel, copy out, all on the current stream.
+* ``attention_from_host(...)`` / ``mlp_from_host(...)`` -- the same
+  operators fed from (pinned) host tensors: copies in, kernels, copies out,
+  pipelined over streams.
 
 Errors: argument problems Python can see (device, dtype, rank) raise
 ``TypeError``/``ValueError``; everything the C ABI rejects raises
@@ -228,6 +229,66 @@ def attention_from_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         s_out.wait_event(ws["ev_cmp"][c])
         with torch.cuda.stream(s_out):
             ho[:, a:z].copy_(ws["o"][:, a:z], non_blocking=True)
+    ws["ev_out"].record(s_out)
+    cur.wait_event(ws["ev_out"])
+    return out
+
+
+def mlp_from_host(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                  act: str = "gelu_tanh", out: torch.Tensor | None = None,
+                  workspace: dict | None = None, chunks: int = 4) -> torch.Tensor:
+    """``mlp`` for a host ``x [M, K]`` with device-resident weights (the serving
+    shape: weights loaded once, activations streamed): host-to-device copy of
+    x, the two GEMMs, device-to-host copy of y.  The rows are split into
+    ``chunks`` blocks (multiples of 128 rows) that flow through copy-in /
+    compute / copy-out streams chained by events, so both PCIe directions
+    overlap the GEMMs; the current stream waits for the last copy out.  Host
+    tensors should be pinned; ``out`` is allocated pinned if omitted;
+    ``workspace`` (a dict) keeps device buffers, streams and events."""
+    _check_cuda_bf16("w1", w1)
+    _check_cuda_bf16("w2", w2)
+    if x.is_cuda or x.dtype != _BF16 or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous 2-D bfloat16 host tensor")
+    dev = w1.device
+    M, K = x.shape
+    N = w1.shape[1]
+    tiles = (M + 127) // 128
+    nch = max(1, min(int(chunks), tiles))
+    bounds = [min(M, 128 * (tiles * i // nch)) for i in range(nch + 1)]
+    ws = workspace if workspace is not None else {}
+    key = (M, K, N, dev, nch)
+    if ws.get("key") != key:
+        for st in ws.get("streams", ()):
+            st.synchronize()
+        ws.clear()
+        ws["key"] = key
+        ws["x"] = torch.empty((M, K), dtype=_BF16, device=dev)
+        ws["h"] = torch.empty((M, N), dtype=_BF16, device=dev)
+        ws["y"] = torch.empty((M, K), dtype=_BF16, device=dev)
+        ws["streams"] = [torch.cuda.Stream(device=dev) for _ in range(3)]
+        ws["ev_in"] = [torch.cuda.Event() for _ in range(nch)]
+        ws["ev_cmp"] = [torch.cuda.Event() for _ in range(nch)]
+        ws["ev_out"] = torch.cuda.Event()
+    if out is None:
+        out = torch.empty((M, K), dtype=_BF16, pin_memory=True)
+    s_in, s_cmp, s_out = ws["streams"]
+    cur = torch.cuda.current_stream(dev)
+    for st in (s_in, s_cmp, s_out):
+        st.wait_stream(cur)
+    for c in range(nch):
+        a, z = bounds[c], bounds[c + 1]
+        if a == z:
+            continue
+        with torch.cuda.stream(s_in):
+            ws["x"][a:z].copy_(x[a:z], non_blocking=True)
+            ws["ev_in"][c].record(s_in)
+        s_cmp.wait_event(ws["ev_in"][c])
+        with torch.cuda.stream(s_cmp):
+            mlp(ws["x"][a:z], w1, w2, act=act, hidden=ws["h"][a:z], out=ws["y"][a:z])
+            ws["ev_cmp"][c].record(s_cmp)
+        s_out.wait_event(ws["ev_cmp"][c])
+        with torch.cuda.stream(s_out):
+            out[a:z].copy_(ws["y"][a:z], non_blocking=True)
     ws["ev_out"].record(s_out)
     cur.wait_event(ws["ev_out"])
     return out

@@ -17,7 +17,8 @@ import torch
 from conftest import GOLDEN, assert_close
 import oracle
 from oracle.mlp import round_to_bf16
-from cs348k_fast_attention_grammar_b200 import FaError, gemm_act, layer_norm_rows, mlp, mlp_ln
+from cs348k_fast_attention_grammar_b200 import (FaError, gemm_act, layer_norm_rows, mlp,
+                                                mlp_from_host, mlp_ln)
 from cs348k_fast_attention_grammar_b200.inputs import MLP_CONFIGS, make_mlp
 
 pytestmark = pytest.mark.gpu
@@ -138,3 +139,19 @@ def test_mlp_ln_block_larger_shape():
     h = round_to_bf16(np.maximum(X @ W1, 0)).astype(np.float64)
     r = round_to_bf16(h @ W2 + X).astype(np.float64)
     assert_close(out, _ln_np(r), what="mlp_ln 384x512x1024")
+
+
+@pytest.mark.parametrize("M,chunks", [(1000, 4), (384, 8), (128, 1)])
+def test_mlp_from_host_matches_device_call(M, chunks):
+    """Row-chunked, stream-pipelined host path == one device call, bit for bit
+    (and again on the second call, reusing the workspace)."""
+    K, N = 256, 512
+    x = _rand((M, K), 21).pin_memory()
+    w1 = _rand((K, N), 22, std=K ** -0.5).to(DEV)
+    w2 = _rand((N, K), 23, std=N ** -0.5).to(DEV)
+    ws = {}
+    for _ in range(2):
+        y_host = mlp_from_host(x, w1, w2, act="gelu_tanh", workspace=ws, chunks=chunks)
+        torch.cuda.synchronize()
+        y_dev = mlp(x.to(DEV), w1, w2, act="gelu_tanh")
+        assert torch.equal(y_host, y_dev.cpu())
