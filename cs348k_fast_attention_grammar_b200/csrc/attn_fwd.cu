@@ -73,6 +73,11 @@ constexpr float kRescaleThreshold = 8.0f;
 #ifndef FA_ATTN_SPLIT_P
 #define FA_ATTN_SPLIT_P 1
 #endif
+// Paired fp32 ops in the exponential loop: bit 0 = scale-and-subtract as one
+// fma.f32x2 per two scores, bit 1 = row sums accumulated with add.f32x2.
+#ifndef FA_ATTN_F2
+#define FA_ATTN_F2 3
+#endif
 // 1 = the two softmax warpgroups take turns on their exp phases (per D).
 #ifndef FA_ATTN_PINGPONG_D64
 #define FA_ATTN_PINGPONG_D64 1
@@ -504,19 +509,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 3);
       const float neg_m = -m_ref;
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
+      uint64_t rs2[2] = {0ull, 0ull};
+      const uint64_t sl2x2 = f2_pack(sl2, sl2);
+      const uint64_t negm2 = f2_pack(neg_m, neg_m);
       uint32_t pk[2][32];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
 #pragma unroll
         for (int cc = 0; cc < 32; ++cc) {
           const int c = half * 32 + cc;
-          const float x0 = fmaf(__uint_as_float(sr[2 * c]), sl2, neg_m);
-          const float x1 = fmaf(__uint_as_float(sr[2 * c + 1]), sl2, neg_m);
+          float x0, x1;
+          if (FA_ATTN_F2 & 1) {
+            // x = s * scale - m for two scores in one paired FMA
+            f2_unpack(ffma2(f2_pack(__uint_as_float(sr[2 * c]), __uint_as_float(sr[2 * c + 1])),
+                            sl2x2, negm2),
+                      x0, x1);
+          } else {
+            x0 = fmaf(__uint_as_float(sr[2 * c]), sl2, neg_m);
+            x1 = fmaf(__uint_as_float(sr[2 * c + 1]), sl2, neg_m);
+          }
           // A fixed share of the pairs goes to the FMA pipe, the rest to MUFU.
           const bool emu = (kEmuMod > 0) && (c % (kEmuMod > 0 ? kEmuMod : 1) == kEmuMod - 1);
           const float p0 = emu ? exp2_fma(x0) : ex2_approx(x0);
           const float p1 = emu ? exp2_fma(x1) : ex2_approx(x1);
-          rs[c & 3] += p0 + p1;
+          if (FA_ATTN_F2 & 2)
+            rs2[c & 1] = fadd2(rs2[c & 1], f2_pack(p0, p1));
+          else
+            rs[c & 3] += p0 + p1;
           pk[half][cc] = kPackAlu ? pack_bf16x2_alu(p0, p1) : pack_bf16x2(p0, p1);
         }
         if (FA_ATTN_SPLIT_P && half == 0) {
@@ -529,7 +548,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (pingpong) mbar_arrive(bar_turn(1 - t));
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 4);
-      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+      if (FA_ATTN_F2 & 2) {
+        float a0, a1, b0, b1;
+        f2_unpack(rs2[0], a0, a1);
+        f2_unpack(rs2[1], b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      } else {
+        l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+      }
       if (!FA_ATTN_SPLIT_P) tmem_st32(tS, pk[0]);
       tmem_st32(tS + 32, pk[1]);
       tmem_wait_st();
