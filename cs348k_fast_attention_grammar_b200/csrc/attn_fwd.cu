@@ -78,6 +78,10 @@ constexpr float kRescaleThreshold = 8.0f;
 #ifndef FA_ATTN_F2
 #define FA_ATTN_F2 3
 #endif
+// 1 = FMA-pipe exponentials computed two at a time (exp2_fma_x2).
+#ifndef FA_ATTN_EMU2
+#define FA_ATTN_EMU2 1
+#endif
 // 1 = the two softmax warpgroups take turns on their exp phases (per D).
 #ifndef FA_ATTN_PINGPONG_D64
 #define FA_ATTN_PINGPONG_D64 1
@@ -110,6 +114,25 @@ __device__ __forceinline__ float exp2_fma(float x) {
   const float f = __fsub_rn(x, j);
   const float p = fmaf(fmaf(fmaf(kExpC3, f, kExpC2), f, kExpC1), f, kExpC0);
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// exp2_fma on two values at once: the same steps and roundings, with the
+// floating-point ones paired (add.f32x2 / fma.f32x2; x - j as an exactly
+// rounded fma with -1), so an emulated pair costs 12 instructions instead
+// of 18.
+__device__ __forceinline__ void exp2_fma_x2(float x0, float x1, float& r0, float& r1) {
+  const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t t = fadd2(x, f2_pack(12582912.f, 12582912.f));
+  const uint64_t j = fadd2(t, f2_pack(-12582912.f, -12582912.f));
+  const uint64_t f = ffma2(j, f2_pack(-1.f, -1.f), x);
+  uint64_t q = ffma2(f2_pack(kExpC3, kExpC3), f, f2_pack(kExpC2, kExpC2));
+  q = ffma2(q, f, f2_pack(kExpC1, kExpC1));
+  q = ffma2(q, f, f2_pack(kExpC0, kExpC0));
+  float p0, p1, t0, t1;
+  f2_unpack(q, p0, p1);
+  f2_unpack(t, t0, t1);
+  r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 // Two non-negative finite fp32 -> bf16x2 (low half = lo) with integer ops:
@@ -530,8 +553,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // A fixed share of the pairs goes to the FMA pipe, the rest to MUFU.
           const bool emu = (kEmuMod > 0) && (c % (kEmuMod > 0 ? kEmuMod : 1) == kEmuMod - 1);
-          const float p0 = emu ? exp2_fma(x0) : ex2_approx(x0);
-          const float p1 = emu ? exp2_fma(x1) : ex2_approx(x1);
+          float p0, p1;
+          if (emu && FA_ATTN_EMU2) {
+            exp2_fma_x2(x0, x1, p0, p1);
+          } else {
+            p0 = emu ? exp2_fma(x0) : ex2_approx(x0);
+            p1 = emu ? exp2_fma(x1) : ex2_approx(x1);
+          }
           if (FA_ATTN_F2 & 2)
             rs2[c & 1] = fadd2(rs2[c & 1], f2_pack(p0, p1));
           else
