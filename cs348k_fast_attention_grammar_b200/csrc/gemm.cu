@@ -37,7 +37,10 @@ constexpr int kGBarOff = kGStages * kStageBytes;
 constexpr int kGNumBars = 2 * kGStages + 4 + 1;     // full, empty, acc_full[2], acc_empty[2], drain
 constexpr int kGMiscOff = kGBarOff + kGNumBars * 8;
 constexpr int kGSmemBytes = kGMiscOff + 16 + 1024;
-constexpr int kGroupM = 8;                          // tile raster: 8 M-tiles per band
+#ifndef FA_GEMM_GROUP_M
+#define FA_GEMM_GROUP_M 8
+#endif
+constexpr int kGroupM = FA_GEMM_GROUP_M;            // tile raster: M-tiles per band
 
 struct GemmParams {
   int M, N, K;
