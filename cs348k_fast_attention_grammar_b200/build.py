@@ -11,6 +11,7 @@ time (tensor maps are encoded through cudaGetDriverEntryPoint).
 from __future__ import annotations
 
 import argparse
+import fcntl
 import os
 import shutil
 import subprocess
@@ -49,21 +50,35 @@ def is_stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile the library if it is missing or older than its sources."""
+    """Compile the library if it is missing or older than its sources.
+
+    Safe when several processes (the ranks of one job) call it at once: an
+    exclusive lock on a file beside the library lets one of them compile, the
+    others wait and then find the library fresh; each compile writes its own
+    temporary file and renames it over the library atomically."""
     if not force and not is_stale():
         return LIB_PATH
-    tmp = LIB_PATH + ".tmp"
-    cmd = ([nvcc_path()] + ARCH_FLAGS + NVCC_FLAGS +
-           [os.path.join(CSRC, s) for s in SOURCES] + ["-o", tmp])
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd), file=sys.stderr)
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if verbose or r.returncode != 0:
-        sys.stderr.write(r.stdout + r.stderr)
-    if r.returncode != 0:
-        raise RuntimeError(f"nvcc failed with exit code {r.returncode}")
-    os.replace(tmp, LIB_PATH)
+    with open(LIB_PATH + ".lock", "a+") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if not force and not is_stale():
+                return LIB_PATH          # another process built it meanwhile
+            tmp = f"{LIB_PATH}.{os.getpid()}.tmp"
+            cmd = ([nvcc_path()] + ARCH_FLAGS + NVCC_FLAGS +
+                   [os.path.join(CSRC, s) for s in SOURCES] + ["-o", tmp])
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+                print(" ".join(cmd), file=sys.stderr)
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if verbose or r.returncode != 0:
+                sys.stderr.write(r.stdout + r.stderr)
+            if r.returncode != 0:
+                if os.path.exists(tmp):
+                    os.unlink(tmp)
+                raise RuntimeError(f"nvcc failed with exit code {r.returncode}")
+            os.replace(tmp, LIB_PATH)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
     return LIB_PATH
 
 
