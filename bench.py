@@ -55,6 +55,8 @@ def parse_args(argv=None):
                                                + ["ref512"]),
                     default="cfg2")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="(batch, head) chunks pipelined over the copy/kernel streams")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--verify-pairs", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -446,7 +448,8 @@ def attention_e2e(args, fab, cfg, q, k, v, world, device, flops_total):
     oh = torch.empty(q.shape, dtype=torch.bfloat16, pin_memory=True)
     ws = {}
     step = lambda: fab.attention_from_host(qh, kh, vh, causal=cfg["causal"], out=oh,  # noqa
-                                           device=device, workspace=ws)
+                                           device=device, workspace=ws,
+                                           chunks=args.e2e_chunks)
     step()
     torch.cuda.synchronize()
     steps = max(1, args.e2e_steps)
@@ -455,7 +458,8 @@ def attention_e2e(args, fab, cfg, q, k, v, world, device, flops_total):
             "steps": steps, "h2d_bytes_per_step": 3 * q.numel() * 2 * world,
             "d2h_bytes_per_step": q.numel() * 2 * world,
             "path": "attention_from_host: pinned host -> device -> host, (batch, head) pairs "
-                    "in 8 chunks pipelined over copy-in / kernel / copy-out streams"}
+                    f"in {args.e2e_chunks} chunks pipelined over copy-in / kernel / copy-out "
+                    "streams"}
 
 
 # The reference's own problem and its published numbers (NVIDIA L4, fp32,
