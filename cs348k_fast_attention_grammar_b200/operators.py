@@ -99,6 +99,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
             raise ValueError("out must match q's shape and device")
     if scale is None:
         scale = 1.0 / math.sqrt(D)
+    if B * H * S == 0:
+        return out                 # empty batch, heads or sequence: nothing to compute
     lib = _lib.load()
     strides = (ctypes.c_int64 * 16)(*q.stride(), *k.stride(), *v.stride(), *out.stride())
     with _on_device(q.device):

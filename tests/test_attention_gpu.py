@@ -218,3 +218,31 @@ def test_property_key_permutation_invariance():
     o1 = attention(q, k, v).float()
     o2 = attention(q, k[:, :, perm].contiguous(), v[:, :, perm].contiguous()).float()
     assert (o1 - o2).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("shape", [(0, 2, 128, 64), (1, 0, 128, 128), (2, 3, 0, 64)])
+def test_empty_inputs_return_empty_output(shape):
+    """Like torch SDPA, an empty batch, head or sequence axis gives an empty
+    result (no launch, no error)."""
+    q = torch.empty(shape, dtype=torch.bfloat16, device=DEV)
+    o = attention(q, q, q, causal=True)
+    assert tuple(o.shape) == shape
+
+
+@pytest.mark.parametrize("D,causal", [(64, True), (128, False)])
+def test_long_sequence_one_pair(D, causal):
+    """S = 65536 (512 key blocks, 256 units per head): rows spread over the
+    sequence against a torch fp32 reference, plus finiteness everywhere."""
+    S = 65536
+    q, k, v = (_rand((1, 1, S, D), 80 + i, amp=0.5).to(DEV) for i in range(3))
+    o = attention(q, k, v, causal=causal)
+    torch.cuda.synchronize()
+    assert torch.isfinite(o.float()).all()
+    qf, kf, vf = q[0, 0].float(), k[0, 0].float(), v[0, 0].float()
+    rows = torch.tensor([0, 1, 127, 128, 4095, 30000, 65535], device=DEV)
+    s = (qf[rows] @ kf.t()) / math.sqrt(D)
+    if causal:
+        s = s.masked_fill(torch.arange(S, device=DEV)[None, :] > rows[:, None], float("-inf"))
+    ref = torch.softmax(s, dim=-1) @ vf
+    d = (o[0, 0, rows].float() - ref).abs()
+    assert d.max().item() <= 2e-2 and d.mean().item() <= 2e-3, d.max().item()
