@@ -312,6 +312,8 @@ def gemm_act(a: torch.Tensor, b: torch.Tensor, act: str = "none",
     N = b.shape[1]
     if out is None:
         out = torch.empty((M, N), dtype=_BF16, device=a.device)
+    if M == 0:
+        return out                 # no rows: nothing to compute
     lib = _lib.load()
     with _on_device(a.device):
         rc = lib.fa_gemm_act(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
@@ -342,6 +344,8 @@ def mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, act: str = "gelu_ta
         hidden = torch.empty((M, N), dtype=_BF16, device=x.device)
     if out is None:
         out = torch.empty((M, K), dtype=_BF16, device=x.device)
+    if M == 0:
+        return out                 # no rows: nothing to compute
     lib = _lib.load()
     with _on_device(x.device):
         rc = lib.fa_mlp_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), hidden.data_ptr(),
@@ -371,6 +375,8 @@ def mlp_ln(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, eps: float = 1e-
     hidden = torch.empty((M, N), dtype=_BF16, device=x.device) if hidden is None else hidden
     resid = torch.empty((M, K), dtype=_BF16, device=x.device) if resid is None else resid
     out = torch.empty((M, K), dtype=_BF16, device=x.device) if out is None else out
+    if M == 0:
+        return out                 # no rows: nothing to compute
     lib = _lib.load()
     with _on_device(x.device):
         rc = lib.fa_mlp_ln_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), hidden.data_ptr(),
@@ -389,6 +395,8 @@ def layer_norm_rows(x: torch.Tensor, eps: float = 1e-5,
         raise ValueError("x must be 2-D with a contiguous last dimension")
     M, N = x.shape
     out = torch.empty((M, N), dtype=_BF16, device=x.device) if out is None else out
+    if M == 0:
+        return out                 # no rows: nothing to compute
     lib = _lib.load()
     with _on_device(x.device):
         rc = lib.fa_layernorm_rows(x.data_ptr(), out.data_ptr(), M, N, x.stride(0),

@@ -155,3 +155,13 @@ def test_mlp_from_host_matches_device_call(M, chunks):
         torch.cuda.synchronize()
         y_dev = mlp(x.to(DEV), w1, w2, act="gelu_tanh")
         assert torch.equal(y_host, y_dev.cpu())
+
+
+def test_empty_rows_return_empty_outputs():
+    x = torch.empty((0, 256), dtype=torch.bfloat16, device=DEV)
+    w1 = _rand((256, 512), 31).to(DEV)
+    w2 = _rand((512, 256), 32).to(DEV)
+    assert tuple(mlp(x, w1, w2).shape) == (0, 256)
+    assert tuple(mlp_ln(x, w1, w2).shape) == (0, 256)
+    assert tuple(gemm_act(x, w1).shape) == (0, 512)
+    assert tuple(layer_norm_rows(x).shape) == (0, 256)
