@@ -665,6 +665,390 @@ int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
+// D = 64 kernel: four 128-row Q tiles per CTA (512 query rows) and 64-key
+// blocks, so four independent S -> softmax -> P -> O += P V chains share the
+// SM (the two-tile kernel above leaves MUFU, tensor pipe and issue slots all
+// half idle at D = 64: each tile's chain latency, not a unit, bounds it).
+// TMEM fits four tiles at D = 64 (4 x 64 S + 4 x 64 O columns) but not at
+// D = 128.  20 warps: 0-15 softmax (tile w >> 2, lane quarter w & 3), 16 TMA
+// producer, 17 TMEM allocator + MMA issuer, 18-19 idle.
+// TMEM: S_t at 64 t (P_t over its first 32 columns), O_t at 256 + 64 t.
+constexpr int kQ4Threads = 640;
+constexpr int kQ4BN = 64;
+
+struct AttnQ4Cfg {
+  static constexpr int kTileBytes = kBM * 64 * 2;          // Q tile, 16 KiB
+  static constexpr int kKVBytes = kQ4BN * 64 * 2;          // K or V block, 8 KiB
+  static constexpr int kStages = 16;
+  static constexpr int kQOff = 0;
+  static constexpr int kKVOff = 4 * kTileBytes;
+  static constexpr int kBarOff = kKVOff + kStages * kKVBytes;
+  // q, kv_full[16], kv_empty[16], s_full[4], p_full[4], o_full[4], drain
+  static constexpr int kNumBars = 1 + 2 * kStages + 12 + 1;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
+  __device__ static constexpr uint32_t col_s(int t) { return 64u * t; }
+  __device__ static constexpr uint32_t col_o(int t) { return 256u + 64u * t; }
+};
+
+template <bool CAUSAL, bool OUT_F32>
+__global__ void __launch_bounds__(kQ4Threads, 1)
+    attn_fwd_q4_kernel(const __grid_constant__ CUtensorMap tmQ,
+                       const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using C = AttnQ4Cfg;
+  constexpr int D = 64;
+  constexpr int kNT = 4;
+  constexpr int kEmuMod = FA_ATTN_EMU_MOD_D64;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sQ = base + C::kQOff;
+  const uint32_t sKV = base + C::kKVOff;
+  const uint32_t bars = base + C::kBarOff;
+  const uint32_t bar_q = bars;
+  auto bar_kv_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto bar_kv_empty = [&](int s) { return bars + 8u * (1 + C::kStages + s); };
+  constexpr int kB0 = 1 + 2 * C::kStages;
+  auto bar_s_full = [&](int t) { return bars + 8u * (kB0 + t); };
+  auto bar_p_full = [&](int t) { return bars + 8u * (kB0 + 4 + t); };
+  auto bar_o_full = [&](int t) { return bars + 8u * (kB0 + 8 + t); };
+  const uint32_t bar_drain = bars + 8u * (kB0 + 12);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + C::kMiscOff + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  int heads_here, first_bh, r_in;
+  {
+    const int big_units = (p.group_q + 1) * p.n_units_per_head;
+    const int big_span = p.group_r * big_units;
+    if (static_cast<int>(blockIdx.x) < big_span) {
+      const int g = blockIdx.x / big_units;
+      r_in = blockIdx.x - g * big_units;
+      heads_here = p.group_q + 1;
+      first_bh = g * heads_here;
+    } else {
+      const int x = blockIdx.x - big_span;
+      const int small_units = p.group_q * p.n_units_per_head;
+      const int g = x / small_units;
+      r_in = x - g * small_units;
+      heads_here = p.group_q;
+      first_bh = p.group_r * (p.group_q + 1) + g * p.group_q;
+    }
+  }
+  int qu = r_in / heads_here;
+  const int bh = first_bh + (r_in - qu * heads_here);
+  if (CAUSAL) qu = p.n_units_per_head - 1 - qu;
+  const int b = bh / p.H;
+  const int h = bh - b * p.H;
+  const int q0 = qu * kNT * kBM;
+  int nt[kNT];
+#pragma unroll
+  for (int t = 0; t < kNT; ++t) {
+    const int qs = q0 + t * kBM;
+    if (qs >= p.S) nt[t] = 0;
+    else if (CAUSAL) nt[t] = min(p.nkv, (qs + kBM - 1) / kQ4BN + 1);
+    else nt[t] = p.nkv;
+  }
+  int n = 0;
+#pragma unroll
+  for (int t = 0; t < kNT; ++t) n = max(n, nt[t]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(bar_kv_full(s), 1);
+      mbar_init(bar_kv_empty(s), 1);
+    }
+    for (int t = 0; t < kNT; ++t) {
+      mbar_init(bar_s_full(t), 1);
+      mbar_init(bar_p_full(t), kBM);
+      mbar_init(bar_o_full(t), 1);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 17) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp == 16 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 16) {
+    // =================== TMA producer ===================
+    if (elect_one()) {
+      const uint64_t pol_q = l2_policy_evict_first();
+      const uint64_t pol_kv = l2_policy_evict_last();
+      int ntiles = 0;
+#pragma unroll
+      for (int t = 0; t < kNT; ++t) ntiles += (nt[t] > 0) ? 1 : 0;
+      mbar_arrive_expect_tx(bar_q, ntiles * C::kTileBytes);
+#pragma unroll
+      for (int t = 0; t < kNT; ++t)
+        if (nt[t] > 0)
+          tma_load_4d(sQ + t * C::kTileBytes, &tmQ, bar_q, 0, q0 + t * kBM, h, b, pol_q);
+      int issued = 0;
+      for (int i = 0; i < 2 * n; ++i) {
+        const int s = i % C::kStages;
+        const uint32_t ph = (i / C::kStages) & 1;
+        if (!mbar_wait(bar_kv_empty(s), ph ^ 1u, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(bar_kv_full(s), C::kKVBytes);
+        const void* map = (i & 1) ? static_cast<const void*>(&tmV)
+                                  : static_cast<const void*>(&tmK);
+        tma_load_4d(sKV + s * C::kKVBytes, map, bar_kv_full(s), 0, (i >> 1) * kQ4BN, h, b,
+                    pol_kv);
+        ++issued;
+      }
+      if (*abort_flag) {
+        drain_wait(bar_q, 0);
+        for (int i = max(0, issued - C::kStages); i < issued; ++i)
+          drain_wait(bar_kv_full(i % C::kStages), (i / C::kStages) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 17) {
+    // =================== MMA issuer ===================
+    // Per block j, for t = 0..3: O_t += P_t(j-1) V_{j-1}, then S_t = Q_t K_j^T.
+    if (elect_one()) {
+      constexpr uint32_t kIdQK = idesc_bf16_f32(kBM, kQ4BN, false, false);
+      constexpr uint32_t kIdPV = idesc_bf16_f32(kBM, D, false, true);
+      bool ok = mbar_wait(bar_q, 0, abort_flag, p.status);
+      tc_fence_after();
+      int vslot = 0;
+      for (int j = 0; ok && j <= n; ++j) {
+        int kslot = 0;
+        if (j < n) {
+          const int i = 2 * j;
+          kslot = i % C::kStages;
+          if (!mbar_wait(bar_kv_full(kslot), (i / C::kStages) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int t = 0; t < kNT; ++t) {
+          if (j >= 1 && j - 1 < nt[t]) {
+            if (!mbar_wait(bar_p_full(t), (j - 1) & 1, abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t vbase = sKV + vslot * C::kKVBytes;
+#pragma unroll
+            for (int kk = 0; kk < kQ4BN / 16; ++kk) {
+              const uint64_t bdesc = sdesc_sw128(vbase + kk * 2048, kQ4BN * 128, 1024);
+              mma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8, bdesc, kIdPV,
+                     (j - 1 > 0 || kk > 0) ? 1u : 0u);
+            }
+            if (j - 1 == nt[t] - 1) mma_commit(bar_o_full(t));
+          }
+          if (j < nt[t]) {
+            const uint32_t qbase = sQ + t * C::kTileBytes;
+            const uint32_t kbase = sKV + kslot * C::kKVBytes;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              mma_ss(tmem + C::col_s(t), sdesc_sw128(qbase + kk * 32, 16, 1024),
+                     sdesc_sw128(kbase + kk * 32, 16, 1024), kIdQK, kk > 0 ? 1u : 0u);
+            mma_commit(bar_s_full(t));
+          }
+        }
+        if (!ok) break;
+        if (j >= 1) mma_commit(bar_kv_empty(vslot));
+        if (j < n) {
+          mma_commit(bar_kv_empty(kslot));
+          const int i = 2 * j + 1;
+          vslot = i % C::kStages;
+          if (!mbar_wait(bar_kv_full(vslot), (i / C::kStages) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+      }
+      mma_commit(bar_drain);
+      drain_wait(bar_drain, 0);
+    }
+    __syncwarp();
+  } else if (warp < 16) {
+    // =================== softmax / epilogue (one tile) ===================
+    const int t = warp >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const int qi = q0 + t * kBM + row;
+    const int q_tile0 = q0 + t * kBM;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_off + C::col_s(t);
+    const uint32_t tO = tmem + lane_off + C::col_o(t);
+    const float sl2 = p.scale_log2;
+    float m_ref = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    auto wwait = [&](uint32_t bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status));
+    };
+    const int my_nt = nt[t];
+    for (int j = 0; j < my_nt; ++j) {
+      if (!wwait(bar_s_full(t), j & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int k0 = j * kQ4BN;
+      const bool need_mask = (k0 + kQ4BN > p.S) || (CAUSAL && (k0 + kQ4BN - 1 > q_tile0));
+      const int lim = CAUSAL ? min(qi + 1, p.S) : p.S;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        uint32_t r[32];
+        tmem_ld32_wait(tS + 32 * ch, r);
+        if (need_mask) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (k0 + 32 * ch + c >= lim) r[c] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int c = 0; c < 32; c += 8)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            mx4[i] = fmax3(mx4[i], __uint_as_float(r[c + 2 * i]), __uint_as_float(r[c + 2 * i + 1]));
+      }
+      const float m_blk = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+      const bool need = (m_ref == -INFINITY) ? (m_blk > -INFINITY)
+                                             : (m_blk - m_ref > kRescaleThreshold);
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_use = need ? m_blk : m_ref;
+        const float alpha = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - m_use);
+        if (j > 0) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t o[32];
+            tmem_ld32_wait(tO + c * 32, o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+        l *= alpha;
+        m_ref = m_use;
+      }
+      const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
+      const uint64_t sl2x2 = f2_pack(sl2, sl2);
+      const uint64_t negm2 = f2_pack(neg_m, neg_m);
+      uint64_t rs2[2] = {0ull, 0ull};
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        uint32_t r[32];
+        tmem_ld32_wait(tS + 32 * ch, r);
+        if (need_mask) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (k0 + 32 * ch + c >= lim) r[c] = __float_as_uint(-INFINITY);
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          float x0, x1;
+          f2_unpack(ffma2(f2_pack(__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1])),
+                          sl2x2, negm2),
+                    x0, x1);
+          const int pair = 16 * ch + c;
+          const bool emu = (kEmuMod > 0) && (pair % (kEmuMod > 0 ? kEmuMod : 1) == kEmuMod - 1);
+          float p0, p1;
+          if (emu) {
+            exp2_fma_x2(x0, x1, p0, p1);
+          } else {
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
+          }
+          rs2[c & 1] = fadd2(rs2[c & 1], f2_pack(p0, p1));
+          pk[c] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(tS + 16 * ch, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar_p_full(t));
+      float a0, a1, b0, b1;
+      f2_unpack(rs2[0], a0, a1);
+      f2_unpack(rs2[1], b0, b1);
+      l += (a0 + a1) + (b0 + b1);
+    }
+    if (ok && my_nt > 0 && wwait(bar_o_full(t), 0)) {
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      const int64_t orow_off = static_cast<int64_t>(b) * p.o_sb +
+                               static_cast<int64_t>(h) * p.o_sh + static_cast<int64_t>(qi) * p.o_ss;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o[32];
+        tmem_ld32_wait(tO + c * 32, o);
+        if (qi < p.S) {
+          if (OUT_F32) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<float*>(p.o) + orow_off + c * 32);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              dst[e] = make_uint4(__float_as_uint(__uint_as_float(o[4 * e]) * inv_l),
+                                  __float_as_uint(__uint_as_float(o[4 * e + 1]) * inv_l),
+                                  __float_as_uint(__uint_as_float(o[4 * e + 2]) * inv_l),
+                                  __float_as_uint(__uint_as_float(o[4 * e + 3]) * inv_l));
+          } else {
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              w[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv_l,
+                                 __uint_as_float(o[2 * e + 1]) * inv_l);
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + orow_off +
+                                                  c * 32);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+            dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 17) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <bool CAUSAL, bool OUT_F32>
+int launch_attn_q4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                   const AttnParams& prm, int grid, cudaStream_t stream) {
+  using C = AttnQ4Cfg;
+  auto kern = attn_fwd_q4_kernel<CAUSAL, OUT_F32>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  int rc = FA_OK;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FA_ERR_CUDA;
+  if (!attr_set[dev]) {
+    rc = prepare_device(reinterpret_cast<const void*>(kern), C::kSmemBytes, &dev);
+    if (rc != FA_OK) return rc;
+    attr_set[dev] = true;
+  }
+  kern<<<grid, kQ4Threads, C::kSmemBytes, stream>>>(mq, mk, mv, prm);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
 }  // namespace
 }  // namespace fa
 
@@ -692,16 +1076,20 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
   int dev = 0;
   int rc = prepare_device(nullptr, 0, &dev);
   if (rc != FA_OK) return rc;
+  // D = 64: four-tile kernel with 64-key blocks; D = 128: two-tile kernel.
+  const bool q4 = (D == 64);
+  const int kv_rows = q4 ? kQ4BN : kBN;                  // keys per K/V block
+  const int unit_rows = q4 ? 4 * kBM : 2 * kBM;          // query rows per CTA
   CUtensorMap mq, mk, mv;
   if ((rc = make_tmap_bhsd(&mq, q, B, H, S, D, st[0], st[1], st[2], kBM)) != FA_OK) return rc;
-  if ((rc = make_tmap_bhsd(&mk, k, B, H, S, D, st[4], st[5], st[6], kBN)) != FA_OK) return rc;
-  if ((rc = make_tmap_bhsd(&mv, v, B, H, S, D, st[8], st[9], st[10], kBN)) != FA_OK) return rc;
+  if ((rc = make_tmap_bhsd(&mk, k, B, H, S, D, st[4], st[5], st[6], kv_rows)) != FA_OK) return rc;
+  if ((rc = make_tmap_bhsd(&mv, v, B, H, S, D, st[8], st[9], st[10], kv_rows)) != FA_OK) return rc;
 
   AttnParams prm;
   prm.B = B;
   prm.H = H;
   prm.S = S;
-  prm.n_units_per_head = (S + 2 * kBM - 1) / (2 * kBM);
+  prm.n_units_per_head = (S + unit_rows - 1) / unit_rows;
   // Groups: at most FA_ATTN_GROUP_MIB of K/V each (>= 1 pair), the pairs
   // split as evenly as possible over them, since a short last group starts its
   // longest units late and leaves a tail.
@@ -716,7 +1104,7 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
     prm.group_q = static_cast<int>(pairs / n_groups);
     prm.group_r = static_cast<int>(pairs % n_groups);
   }
-  prm.nkv = (S + kBN - 1) / kBN;
+  prm.nkv = (S + kv_rows - 1) / kv_rows;
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.o = o;
   prm.o_sb = st[12];
@@ -726,16 +1114,16 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
   prm.trace = g_trace_buffer;
   if (prm.status == nullptr) return FA_ERR_CUDA;
   const int grid = static_cast<int>(static_cast<int64_t>(B) * H * prm.n_units_per_head);
-  if (out_f32) {
-    if (D == 64)
-      return causal ? launch_attn<64, true, true>(mq, mk, mv, prm, grid, stream)
-                    : launch_attn<64, false, true>(mq, mk, mv, prm, grid, stream);
+  if (q4) {
+    if (out_f32)
+      return causal ? launch_attn_q4<true, true>(mq, mk, mv, prm, grid, stream)
+                    : launch_attn_q4<false, true>(mq, mk, mv, prm, grid, stream);
+    return causal ? launch_attn_q4<true, false>(mq, mk, mv, prm, grid, stream)
+                  : launch_attn_q4<false, false>(mq, mk, mv, prm, grid, stream);
+  }
+  if (out_f32)
     return causal ? launch_attn<128, true, true>(mq, mk, mv, prm, grid, stream)
                   : launch_attn<128, false, true>(mq, mk, mv, prm, grid, stream);
-  }
-  if (D == 64)
-    return causal ? launch_attn<64, true, false>(mq, mk, mv, prm, grid, stream)
-                  : launch_attn<64, false, false>(mq, mk, mv, prm, grid, stream);
   return causal ? launch_attn<128, true, false>(mq, mk, mv, prm, grid, stream)
                 : launch_attn<128, false, false>(mq, mk, mv, prm, grid, stream);
 }
