@@ -25,9 +25,11 @@
 // so "S_t(j) complete" implies "O_t holds all blocks < j", which is when the
 // softmax warps may rescale O_t in place.  P is published in two halves (keys
 // 0-63, then 64-127), and O_t += P_t V starts on the first half while the
-// softmax computes the second.  At D = 64 the two softmax warpgroups also take
-// turns on their exponential phases; 25 % of those exponentials run on the
-// FMA pipe.
+// softmax computes the second.
+// This two-tile kernel serves D = 128; D = 64 runs attn_fwd_q4_kernel below
+// (four Q tiles per CTA over 64-key blocks).  The D = 64 branches of the
+// two-tile kernel (exp turns between the warpgroups, FMA-pipe exponentials)
+// remain compilable for comparison but are not dispatched.
 // Scheduling: (batch, head) pairs in groups of <= 32 MiB of K/V (L2-resident),
 // causal units longest first within a group.
 // Online softmax (exp2 domain, log2(e) folded into the scale): the running
