@@ -246,3 +246,36 @@ def test_long_sequence_one_pair(D, causal):
     ref = torch.softmax(s, dim=-1) @ vf
     d = (o[0, 0, rows].float() - ref).abs()
     assert d.max().item() <= 2e-2 and d.mean().item() <= 2e-3, d.max().item()
+
+
+def _random_cases(n=40, seed=2026):
+    rng = np.random.default_rng(seed)
+    cases = []
+    for _ in range(n):
+        D = int(rng.choice([64, 128]))
+        S = int(rng.choice([int(rng.integers(1, 1100)), int(rng.choice([64, 128, 256, 512, 640]))]))
+        B = int(rng.integers(1, 3))
+        H = int(rng.integers(1, 4))
+        causal = bool(rng.integers(0, 2))
+        layout = str(rng.choice(["bhsd", "bshd", "padded"]))
+        cases.append((B, H, S, D, causal, layout))
+    return cases
+
+
+@pytest.mark.parametrize("B,H,S,D,causal,layout", _random_cases())
+def test_attention_random_shapes_and_layouts(B, H, S, D, causal, layout):
+    """Seeded random shapes (ragged S, both head dims, causal or not) and
+    memory layouts: contiguous [B,H,S,D], (B,S,H,D) viewed as [B,H,S,D], and
+    rows padded to a larger sequence stride."""
+    g = torch.Generator().manual_seed(B * 1000003 + H * 1009 + S * 7 + D + int(causal))
+    if layout == "bhsd":
+        mk = lambda: torch.randn((B, H, S, D), generator=g).to(torch.bfloat16)  # noqa: E731
+    elif layout == "bshd":
+        mk = lambda: torch.randn((B, S, H, D), generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)  # noqa
+    else:
+        mk = lambda: torch.randn((B, H, S + 24, D), generator=g).to(torch.bfloat16)[:, :, :S]  # noqa
+    q, k, v = mk(), mk(), mk()
+    out = attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    torch.cuda.synchronize()
+    ref = oracle.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), causal=causal)
+    assert_close(out.float().cpu().numpy(), ref, what=f"{layout} B{B} H{H} S{S} D{D} c={causal}")
