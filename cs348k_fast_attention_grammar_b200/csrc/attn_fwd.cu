@@ -38,6 +38,9 @@
 // for any reference maximum.
 #include <cuda_bf16.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "fa_internal.h"
 #include "sm100_ptx.cuh"
 #include "sm100_tmem_wide.cuh"
@@ -97,6 +100,16 @@ constexpr float kRescaleThreshold = 8.0f;
 #ifndef FA_ATTN_SETMAXNREG
 #define FA_ATTN_SETMAXNREG 1
 #endif
+// 1 = the attention kernels run persistent (one CTA per SM taking units from
+// a global counter) when there are more units than SMs, so a unit's Q and
+// first K/V tiles load, and its first S GEMMs run, while the previous unit
+// ends.
+#ifndef FA_ATTN_PERSIST
+#define FA_ATTN_PERSIST 1
+#endif
+// Counter pairs for persistent launches, handed out round-robin per launch.
+constexpr int kUnitCtrSlots = 1024;
+__device__ unsigned int g_attn_unit_ctr[2 * kUnitCtrSlots];
 
 // Degree-3 minimax (relative error) polynomial for 2^f on [-1/2, 1/2],
 // max relative error 7.5e-5; fitted by fit_exp2_poly.py (Remez exchange).
@@ -164,9 +177,10 @@ struct AttnCfg {
   static constexpr int kKVOff = 2 * kTileBytes;
   static constexpr int kBarOff = kKVOff + kStages * kTileBytes;
   // q_full, kv_full[kStages], kv_empty[kStages], s_full[2], p_full[2],
-  // o_full[2], drain, turn[2], p_half[2]
-  static constexpr int kNumBars = 1 + 2 * kStages + 11;
-  static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem base, abort flag
+  // o_full[2], drain, turn[2], p_half[2], q_empty, unit_full[2], unit_empty[2]
+  static constexpr int kNumBars = 1 + 2 * kStages + 16;
+  // tmem base, abort flag, unit ring (2 ints)
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + alignment slack
   // TMEM column of S_t (P_t aliases its first 64 columns) and of O_t.
   __device__ static constexpr uint32_t col_s(int t) { return 128u * t; }
@@ -184,6 +198,13 @@ struct AttnParams {
   int64_t o_sb, o_sh, o_ss;
   int* status;
   unsigned long long* trace;   // timeline buffer (trace builds only), else null
+  // Persistent launches: units 0..total_units-1; CTA c runs
+  // unit c first, then takes gridDim.x + atomicAdd(unit_ctr[0], 1) until that
+  // passes total_units.  unit_ctr[1] counts finished CTAs; the last one resets
+  // both words to zero for the next launch that uses this counter pair.
+  // Null: one unit per CTA (grid = total_units).
+  int total_units;
+  unsigned int* unit_ctr;
 };
 
 // Optional timeline instrumentation (compiled out unless FA_ATTN_TRACE):
@@ -191,17 +212,30 @@ struct AttnParams {
 // [cta][iteration j][event], events 6t+0..6t+5 softmax tile t (wait start,
 // S ready, row max done, exp turn acquired, exps done, P stored + arrived),
 // 12+2t / 13+2t MMA tile t (P seen, S issued).
+// After those stamps, a per-unit record for the first kCtaTraceMax work units
+// (256 query rows of one head): [SM id, start, first S seen by tile 0, last O
+// ready, end, key blocks], the times from the global nanosecond timer so that
+// units on different SMs line up.
+#ifdef FA_ATTN_TRACE
 constexpr int kTraceCtas = 8;
 constexpr int kTraceEvents = 16;
 constexpr int kTraceIters = 64;
-#ifdef FA_ATTN_TRACE
+constexpr int kCtaTraceMax = 8192;
+constexpr int kCtaTraceFields = 6;
 #define FA_TRACE(j, ev)                                                              \
   do {                                                                               \
     if (p.trace != nullptr && blockIdx.x < kTraceCtas && (j) < kTraceIters)          \
       p.trace[(blockIdx.x * kTraceIters + (j)) * kTraceEvents + (ev)] = clock64();   \
   } while (0)
+#define FA_CTA_TRACE(unit, field, value)                                             \
+  do {                                                                               \
+    if (p.trace != nullptr && (unit) < kCtaTraceMax)                                 \
+      p.trace[kTraceCtas * kTraceIters * kTraceEvents +                              \
+              (unit) * kCtaTraceFields + (field)] = (value);                         \
+  } while (0)
 #else
 #define FA_TRACE(j, ev) do { } while (0)
+#define FA_CTA_TRACE(unit, field, value) do { } while (0)
 #endif
 
 // Bounded drain wait used only on the abort path: returns when the phase
@@ -210,6 +244,47 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
     if (globaltimer_ns() - t0 > 50ull * 1000ull * 1000ull) return;
+  }
+}
+
+// Work unit u of the two-tile kernel: 256 query rows (two 128-row tiles) of
+// one (batch, head) pair.  Pairs are taken in consecutive groups of
+// group_q + 1 (the first group_r groups) or group_q pairs, so the K/V of a
+// group stay resident in L2.  Inside a group the units run
+// query-position-major, and for causal attention the longest (last) query
+// units of every head of the group go first, so the short units fill the
+// tail.  nt[t] = key blocks of tile t (0 when the tile starts past S).
+template <bool CAUSAL>
+__device__ __forceinline__ void decode_unit(const AttnParams& p, int unit, int& b, int& h,
+                                            int& q0, int nt[2]) {
+  int heads_here, first_bh, r_in;
+  const int big_units = (p.group_q + 1) * p.n_units_per_head;
+  const int big_span = p.group_r * big_units;
+  if (unit < big_span) {
+    const int g = unit / big_units;
+    r_in = unit - g * big_units;
+    heads_here = p.group_q + 1;
+    first_bh = g * heads_here;
+  } else {
+    const int x = unit - big_span;
+    const int small_units = p.group_q * p.n_units_per_head;
+    const int g = x / small_units;
+    r_in = x - g * small_units;
+    heads_here = p.group_q;
+    first_bh = p.group_r * (p.group_q + 1) + g * p.group_q;
+  }
+  int qu = r_in / heads_here;
+  const int bh = first_bh + (r_in - qu * heads_here);
+  if (CAUSAL) qu = p.n_units_per_head - 1 - qu;
+  b = bh / p.H;
+  h = bh - b * p.H;
+  q0 = qu * 2 * kBM;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qs = q0 + t * kBM;
+    if (qs >= p.S) nt[t] = 0;
+    else if (CAUSAL) nt[t] = min(p.nkv, qs / kBN + 1);
+    else nt[t] = p.nkv;
   }
 }
 
@@ -239,51 +314,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar_turn = [&](int t) { return bars + 8u * (8 + 2 * C::kStages + t); };
   // p_half[t] completes when the first 64 keys of P_t are in TMEM.
   auto bar_p_half = [&](int t) { return bars + 8u * (10 + 2 * C::kStages + t); };
+  // q_empty completes when a unit's last S GEMMs are done (the Q tiles are free).
+  const uint32_t bar_q_empty = bars + 8u * (12 + 2 * C::kStages);
+  // Unit ring: the producer writes unit_slot[s] and arrives on unit_full[s];
+  // the MMA thread and the eight softmax warps arrive on unit_empty[s] once
+  // they have read it.  -1 ends the CTA's work.
+  auto bar_unit_full = [&](int s) { return bars + 8u * (13 + 2 * C::kStages + s); };
+  auto bar_unit_empty = [&](int s) { return bars + 8u * (15 + 2 * C::kStages + s); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + C::kMiscOff + 4);
+  volatile int* unit_slot = reinterpret_cast<volatile int*>(gbase + C::kMiscOff + 8);
+  constexpr bool kPingPong = (D == 64) ? (FA_ATTN_PINGPONG_D64 != 0) : (FA_ATTN_PINGPONG_D128 != 0);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // ---- work unit ------------------------------------------------------------
-  // (batch, head) pairs are taken in consecutive groups of group_q + 1 (the
-  // first group_r groups) or group_q pairs, so the K/V of a group stay
-  // resident in L2.  Inside a group the units run query-position-major, and
-  // for causal attention the longest (last) query units of every head of the
-  // group go first, so the short units fill the tail.
-  int heads_here, first_bh, r_in;
-  {
-    const int big_units = (p.group_q + 1) * p.n_units_per_head;
-    const int big_span = p.group_r * big_units;
-    if (static_cast<int>(blockIdx.x) < big_span) {
-      const int g = blockIdx.x / big_units;
-      r_in = blockIdx.x - g * big_units;
-      heads_here = p.group_q + 1;
-      first_bh = g * heads_here;
-    } else {
-      const int x = blockIdx.x - big_span;
-      const int small_units = p.group_q * p.n_units_per_head;
-      const int g = x / small_units;
-      r_in = x - g * small_units;
-      heads_here = p.group_q;
-      first_bh = p.group_r * (p.group_q + 1) + g * p.group_q;
-    }
-  }
-  int qu = r_in / heads_here;
-  const int bh = first_bh + (r_in - qu * heads_here);
-  if (CAUSAL) qu = p.n_units_per_head - 1 - qu;
-  const int b = bh / p.H;
-  const int h = bh - b * p.H;
-  const int q0 = qu * 2 * kBM;
-  int nt[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int qs = q0 + t * kBM;
-    if (qs >= p.S) nt[t] = 0;
-    else if (CAUSAL) nt[t] = min(p.nkv, qs / kBN + 1);
-    else nt[t] = p.nkv;
-  }
-  const int n = max(nt[0], nt[1]);
 
   // ---- setup ----------------------------------------------------------------
   if (threadIdx.x == 0) {
@@ -301,6 +345,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_drain, 1);
     mbar_init(bar_turn(0), kBM);
     mbar_init(bar_turn(1), kBM);
+    mbar_init(bar_q_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_unit_full(s), 1);
+      mbar_init(bar_unit_empty(s), 1 + 8);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -328,31 +377,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
-      mbar_arrive_expect_tx(bar_q, 2 * C::kTileBytes);
+      int issued = 0;     // K/V tiles issued, over all units (ring position)
+      int uc = 0;         // units published
+      int unit = blockIdx.x;
+      for (int take = 0;; ++take) {
+        // Publish the unit (or -1) once the ring slot's previous entry is read.
+        const int us = take & 1;
+        if (take >= 2 &&
+            !mbar_wait(bar_unit_empty(us), ((take >> 1) - 1) & 1, abort_flag, p.status))
+          break;
+        const bool done = unit >= p.total_units;
+        unit_slot[us] = done ? -1 : unit;
+        mbar_arrive(bar_unit_full(us));
+        if (done) break;
+        int b, h, q0, nt[2];
+        decode_unit<CAUSAL>(p, unit, b, h, q0, nt);
+        const int n = max(nt[0], nt[1]);
+        // The Q tiles are free once the previous unit's last S GEMMs are done;
+        // this unit's Q and first K/V tiles land while that unit finishes.
+        if (uc > 0 && !mbar_wait(bar_q_empty, (uc - 1) & 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(bar_q, 2 * C::kTileBytes);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+        for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int dk = 0; dk < D / 64; ++dk)
-          tma_load_4d(sQ + t * C::kTileBytes + dk * 16384, &tmQ, bar_q, dk * 64, q0 + t * kBM,
-                      h, b, pol_q);
-      int issued = 0;
-      for (int i = 0; i < 2 * n; ++i) {
-        const int s = i % C::kStages;
-        const uint32_t ph = (i / C::kStages) & 1;
-        if (!mbar_wait(bar_kv_empty(s), ph ^ 1u, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(bar_kv_full(s), C::kTileBytes);
-        const void* map = (i & 1) ? static_cast<const void*>(&tmV)
-                                  : static_cast<const void*>(&tmK);
-        const int j = i >> 1;
+          for (int dk = 0; dk < D / 64; ++dk)
+            tma_load_4d(sQ + t * C::kTileBytes + dk * 16384, &tmQ, bar_q, dk * 64,
+                        q0 + t * kBM, h, b, pol_q);
+        ++uc;
+        bool kv_ok = true;
+        for (int i = 0; i < 2 * n; ++i) {
+          const int s = issued % C::kStages;
+          const uint32_t ph = (issued / C::kStages) & 1;
+          if (!mbar_wait(bar_kv_empty(s), ph ^ 1u, abort_flag, p.status)) {
+            kv_ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar_kv_full(s), C::kTileBytes);
+          const void* map = (i & 1) ? static_cast<const void*>(&tmV)
+                                    : static_cast<const void*>(&tmK);
+          const int j = i >> 1;
 #pragma unroll
-        for (int dk = 0; dk < D / 64; ++dk)
-          tma_load_4d(sKV + s * C::kTileBytes + dk * 16384, map, bar_kv_full(s), dk * 64,
-                      j * kBN, h, b, pol_kv);
-        ++issued;
+          for (int dk = 0; dk < D / 64; ++dk)
+            tma_load_4d(sKV + s * C::kTileBytes + dk * 16384, map, bar_kv_full(s), dk * 64,
+                        j * kBN, h, b, pol_kv);
+          ++issued;
+        }
+        if (!kv_ok) break;
+        if (p.unit_ctr == nullptr) {
+          unit = p.total_units;
+        } else {
+          const unsigned int nx = gridDim.x + atomicAdd(p.unit_ctr, 1u);
+          unit = nx < static_cast<unsigned int>(p.total_units) ? static_cast<int>(nx)
+                                                               : p.total_units;
+        }
       }
       if (*abort_flag) {
         // Let the copies already in flight land before the CTA exits.
-        drain_wait(bar_q, 0);
+        if (uc > 0) drain_wait(bar_q, (uc - 1) & 1);
         for (int i = max(0, issued - C::kStages); i < issued; ++i)
           drain_wait(bar_kv_full(i % C::kStages), (i / C::kStages) & 1);
       }
@@ -363,18 +444,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       constexpr uint32_t kIdQK = idesc_bf16_f32(kBM, kBN, false, false);
       constexpr uint32_t kIdPV = idesc_bf16_f32(kBM, D, false, true);
-      bool ok = mbar_wait(bar_q, 0, abort_flag, p.status);
+      bool ok = true;
+      int it = 0;              // K/V tiles consumed, over all units (ring position)
+      int pb[2] = {0, 0};      // key blocks of tile t in earlier units (P phases)
+      for (int uc = 0; ok; ++uc) {
+      const int us = uc & 1;
+      if (!mbar_wait(bar_unit_full(us), (uc >> 1) & 1, abort_flag, p.status)) break;
+      const int unit = unit_slot[us];
+      mbar_arrive(bar_unit_empty(us));
+      if (unit < 0) break;
+      int b, h, q0, nt[2];
+      decode_unit<CAUSAL>(p, unit, b, h, q0, nt);
+      const int n = max(nt[0], nt[1]);
+      if (!mbar_wait(bar_q, uc & 1, abort_flag, p.status)) break;
       tc_fence_after();
       int vslot = 0;
       for (int j = 0; ok && j <= n; ++j) {
         int kslot = 0;
         if (j < n) {
-          const int i = 2 * j;
-          kslot = i % C::kStages;
-          if (!mbar_wait(bar_kv_full(kslot), (i / C::kStages) & 1, abort_flag, p.status)) {
+          kslot = it % C::kStages;
+          if (!mbar_wait(bar_kv_full(kslot), (it / C::kStages) & 1, abort_flag, p.status)) {
             ok = false;
             break;
           }
+          ++it;
           tc_fence_after();
         }
 #pragma unroll
@@ -389,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // the first half of P is stored, keys 64-127 after the rest.
               if (half == 0 && !FA_ATTN_SPLIT_P) continue;
               const uint32_t bar = (half == 0) ? bar_p_half(t) : bar_p_full(t);
-              if (!mbar_wait(bar, (j - 1) & 1, abort_flag, p.status)) {
+              if (!mbar_wait(bar, (pb[t] + j - 1) & 1, abort_flag, p.status)) {
                 ok = false;
                 break;
               }
@@ -425,14 +518,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j >= 1) mma_commit(bar_kv_empty(vslot));      // V_{j-1} consumed
         if (j < n) {
           mma_commit(bar_kv_empty(kslot));                // K_j consumed
-          const int i = 2 * j + 1;
-          vslot = i % C::kStages;
-          if (!mbar_wait(bar_kv_full(vslot), (i / C::kStages) & 1, abort_flag, p.status)) {
+          if (j == n - 1) mma_commit(bar_q_empty);        // the unit's last S GEMMs
+          vslot = it % C::kStages;
+          if (!mbar_wait(bar_kv_full(vslot), (it / C::kStages) & 1, abort_flag, p.status)) {
             ok = false;
             break;
           }
+          ++it;
           tc_fence_after();
         }
+      }
+      pb[0] += nt[0];
+      pb[1] += nt[1];
       }
       // Every issued MMA (and its commit arrivals) completes before teardown.
       mma_commit(bar_drain);
@@ -448,13 +545,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = warp >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
-    const int qi = q0 + t * kBM + row;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tS = tmem + lane_off + C::col_s(t);
     const uint32_t tO = tmem + lane_off + C::col_o(t);
     const float sl2 = p.scale_log2;
-    float m_ref = -INFINITY;   // reference row max, already scaled (log2 domain)
-    float l = 0.f;             // running row sum of exp2(s * sl2 - m_ref)
     bool ok = true;
     // Warp-uniform bounded wait: every lane waits, and the warp goes on only
     // if all lanes saw the phase complete, so an abort never splits a warp
@@ -462,17 +556,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto wwait = [&](uint32_t bar, uint32_t parity) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status));
     };
+    int sb = 0;   // key blocks of this tile in earlier units (S phases)
+    int ou = 0;   // earlier units in which this tile had work (O phases)
+    for (int uc = 0; ok; ++uc) {
+    const int us = uc & 1;
+    if (!wwait(bar_unit_full(us), (uc >> 1) & 1)) break;
+    const int unit = unit_slot[us];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_unit_empty(us));
+    if (unit < 0) break;
+    int b, h, q0, nt[2];
+    decode_unit<CAUSAL>(p, unit, b, h, q0, nt);
+    if (t == 0 && lane == 0 && wq == 0) {
+      FA_CTA_TRACE(unit, 1, globaltimer_ns());
+      FA_CTA_TRACE(unit, 0, smid());
+      FA_CTA_TRACE(unit, 5, max(nt[0], nt[1]));
+    }
+    const int qi = q0 + t * kBM + row;
+    float m_ref = -INFINITY;   // reference row max, already scaled (log2 domain)
+    float l = 0.f;             // running row sum of exp2(s * sl2 - m_ref)
     const int q_tile0 = q0 + t * kBM;
-    constexpr bool kPingPong = (D == 64) ? (FA_ATTN_PINGPONG_D64 != 0) : (FA_ATTN_PINGPONG_D128 != 0);
+    // The turn phases below count the blocks of one unit, so ping-pong builds
+    // launch one unit per CTA (the host never passes a unit counter to them).
     const bool pingpong = kPingPong && nt[0] > 0 && nt[1] > 0;
     for (int j = 0; j < nt[t]; ++j) {
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 0);
-      if (!wwait(bar_s_full(t), j & 1)) {
+      if (!wwait(bar_s_full(t), (sb + j) & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 1);
+      if (j == 0 && t == 0 && lane == 0 && wq == 0) FA_CTA_TRACE(unit, 2, globaltimer_ns());
       uint32_t sr[128];
       {
         uint32_t r0[32], r1[32], r2[32], r3[32];
@@ -601,8 +716,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       else
         ok = false;
     }
-    if (ok && nt[t] > 0 && wwait(bar_o_full(t), 0)) {
+    if (ok && nt[t] > 0 && wwait(bar_o_full(t), ou & 1)) {
       tc_fence_after();
+      if (t == (nt[1] > 0 ? 1 : 0) && lane == 0 && wq == 0) FA_CTA_TRACE(unit, 3, globaltimer_ns());
       const float inv_l = 1.f / l;
       const int64_t orow_off = static_cast<int64_t>(b) * p.o_sb +
                                static_cast<int64_t>(h) * p.o_sh + static_cast<int64_t>(qi) * p.o_ss;
@@ -637,6 +753,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (t == (nt[1] > 0 ? 1 : 0) && lane == 0 && wq == 0) FA_CTA_TRACE(unit, 4, globaltimer_ns());
+    }
+    if (nt[t] > 0) ++ou;
+    sb += nt[t];
     }
   }
 
@@ -646,6 +766,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0 && p.unit_ctr != nullptr) {
+    // Every fetch of this CTA precedes the barrier above; the last CTA to
+    // finish resets the counter pair for the next launch that uses it.
+    __threadfence();
+    if (atomicAdd(p.unit_ctr + 1, 1u) == gridDim.x - 1) {
+      atomicExch(p.unit_ctr, 0u);
+      atomicExch(p.unit_ctr + 1, 0u);
+    }
   }
 }
 
@@ -685,13 +814,51 @@ struct AttnQ4Cfg {
   static constexpr int kQOff = 0;
   static constexpr int kKVOff = 4 * kTileBytes;
   static constexpr int kBarOff = kKVOff + kStages * kKVBytes;
-  // q, kv_full[16], kv_empty[16], s_full[4], p_full[4], o_full[4], drain
-  static constexpr int kNumBars = 1 + 2 * kStages + 12 + 1;
+  // q, kv_full[16], kv_empty[16], s_full[4], p_full[4], o_full[4], drain,
+  // q_empty, unit_full[2], unit_empty[2]
+  static constexpr int kNumBars = 1 + 2 * kStages + 12 + 1 + 5;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
   __device__ static constexpr uint32_t col_s(int t) { return 64u * t; }
   __device__ static constexpr uint32_t col_o(int t) { return 256u + 64u * t; }
 };
+
+// Work unit u of the four-tile kernel: 512 query rows (four 128-row tiles)
+// of one (batch, head) pair, ordered as decode_unit orders the two-tile
+// kernel's units.  nt[t] = 64-key blocks of tile t (0 past S).
+template <bool CAUSAL>
+__device__ __forceinline__ void decode_unit_q4(const AttnParams& p, int unit, int& b, int& h,
+                                               int& q0, int nt[4]) {
+  int heads_here, first_bh, r_in;
+  const int big_units = (p.group_q + 1) * p.n_units_per_head;
+  const int big_span = p.group_r * big_units;
+  if (unit < big_span) {
+    const int g = unit / big_units;
+    r_in = unit - g * big_units;
+    heads_here = p.group_q + 1;
+    first_bh = g * heads_here;
+  } else {
+    const int x = unit - big_span;
+    const int small_units = p.group_q * p.n_units_per_head;
+    const int g = x / small_units;
+    r_in = x - g * small_units;
+    heads_here = p.group_q;
+    first_bh = p.group_r * (p.group_q + 1) + g * p.group_q;
+  }
+  int qu = r_in / heads_here;
+  const int bh = first_bh + (r_in - qu * heads_here);
+  if (CAUSAL) qu = p.n_units_per_head - 1 - qu;
+  b = bh / p.H;
+  h = bh - b * p.H;
+  q0 = qu * 4 * kBM;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int qs = q0 + t * kBM;
+    if (qs >= p.S) nt[t] = 0;
+    else if (CAUSAL) nt[t] = min(p.nkv, (qs + kBM - 1) / kQ4BN + 1);
+    else nt[t] = p.nkv;
+  }
+}
 
 template <bool CAUSAL, bool OUT_F32>
 __global__ void __launch_bounds__(kQ4Threads, 1)
@@ -717,47 +884,17 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
   auto bar_p_full = [&](int t) { return bars + 8u * (kB0 + 4 + t); };
   auto bar_o_full = [&](int t) { return bars + 8u * (kB0 + 8 + t); };
   const uint32_t bar_drain = bars + 8u * (kB0 + 12);
+  // q_empty: a unit's last S GEMMs are done; unit ring as in attn_fwd_kernel,
+  // read by the MMA thread and the 16 softmax warps.
+  const uint32_t bar_q_empty = bars + 8u * (kB0 + 13);
+  auto bar_unit_full = [&](int s) { return bars + 8u * (kB0 + 14 + s); };
+  auto bar_unit_empty = [&](int s) { return bars + 8u * (kB0 + 16 + s); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + C::kMiscOff + 4);
+  volatile int* unit_slot = reinterpret_cast<volatile int*>(gbase + C::kMiscOff + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  int heads_here, first_bh, r_in;
-  {
-    const int big_units = (p.group_q + 1) * p.n_units_per_head;
-    const int big_span = p.group_r * big_units;
-    if (static_cast<int>(blockIdx.x) < big_span) {
-      const int g = blockIdx.x / big_units;
-      r_in = blockIdx.x - g * big_units;
-      heads_here = p.group_q + 1;
-      first_bh = g * heads_here;
-    } else {
-      const int x = blockIdx.x - big_span;
-      const int small_units = p.group_q * p.n_units_per_head;
-      const int g = x / small_units;
-      r_in = x - g * small_units;
-      heads_here = p.group_q;
-      first_bh = p.group_r * (p.group_q + 1) + g * p.group_q;
-    }
-  }
-  int qu = r_in / heads_here;
-  const int bh = first_bh + (r_in - qu * heads_here);
-  if (CAUSAL) qu = p.n_units_per_head - 1 - qu;
-  const int b = bh / p.H;
-  const int h = bh - b * p.H;
-  const int q0 = qu * kNT * kBM;
-  int nt[kNT];
-#pragma unroll
-  for (int t = 0; t < kNT; ++t) {
-    const int qs = q0 + t * kBM;
-    if (qs >= p.S) nt[t] = 0;
-    else if (CAUSAL) nt[t] = min(p.nkv, (qs + kBM - 1) / kQ4BN + 1);
-    else nt[t] = p.nkv;
-  }
-  int n = 0;
-#pragma unroll
-  for (int t = 0; t < kNT; ++t) n = max(n, nt[t]);
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
@@ -771,6 +908,11 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
       mbar_init(bar_o_full(t), 1);
     }
     mbar_init(bar_drain, 1);
+    mbar_init(bar_q_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_unit_full(s), 1);
+      mbar_init(bar_unit_empty(s), 1 + 16);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -793,28 +935,59 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
     if (elect_one()) {
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
-      int ntiles = 0;
+      int issued = 0;     // K/V blocks issued, over all units (ring position)
+      int uc = 0;         // units published
+      int unit = blockIdx.x;
+      for (int take = 0;; ++take) {
+        const int us = take & 1;
+        if (take >= 2 &&
+            !mbar_wait(bar_unit_empty(us), ((take >> 1) - 1) & 1, abort_flag, p.status))
+          break;
+        const bool done = unit >= p.total_units;
+        unit_slot[us] = done ? -1 : unit;
+        mbar_arrive(bar_unit_full(us));
+        if (done) break;
+        int b, h, q0, nt[kNT];
+        decode_unit_q4<CAUSAL>(p, unit, b, h, q0, nt);
+        int n = 0, ntiles = 0;
 #pragma unroll
-      for (int t = 0; t < kNT; ++t) ntiles += (nt[t] > 0) ? 1 : 0;
-      mbar_arrive_expect_tx(bar_q, ntiles * C::kTileBytes);
+        for (int t = 0; t < kNT; ++t) {
+          n = max(n, nt[t]);
+          ntiles += (nt[t] > 0) ? 1 : 0;
+        }
+        if (uc > 0 && !mbar_wait(bar_q_empty, (uc - 1) & 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(bar_q, ntiles * C::kTileBytes);
 #pragma unroll
-      for (int t = 0; t < kNT; ++t)
-        if (nt[t] > 0)
-          tma_load_4d(sQ + t * C::kTileBytes, &tmQ, bar_q, 0, q0 + t * kBM, h, b, pol_q);
-      int issued = 0;
-      for (int i = 0; i < 2 * n; ++i) {
-        const int s = i % C::kStages;
-        const uint32_t ph = (i / C::kStages) & 1;
-        if (!mbar_wait(bar_kv_empty(s), ph ^ 1u, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(bar_kv_full(s), C::kKVBytes);
-        const void* map = (i & 1) ? static_cast<const void*>(&tmV)
-                                  : static_cast<const void*>(&tmK);
-        tma_load_4d(sKV + s * C::kKVBytes, map, bar_kv_full(s), 0, (i >> 1) * kQ4BN, h, b,
-                    pol_kv);
-        ++issued;
+        for (int t = 0; t < kNT; ++t)
+          if (nt[t] > 0)
+            tma_load_4d(sQ + t * C::kTileBytes, &tmQ, bar_q, 0, q0 + t * kBM, h, b, pol_q);
+        ++uc;
+        bool kv_ok = true;
+        for (int i = 0; i < 2 * n; ++i) {
+          const int s = issued % C::kStages;
+          const uint32_t ph = (issued / C::kStages) & 1;
+          if (!mbar_wait(bar_kv_empty(s), ph ^ 1u, abort_flag, p.status)) {
+            kv_ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar_kv_full(s), C::kKVBytes);
+          const void* map = (i & 1) ? static_cast<const void*>(&tmV)
+                                    : static_cast<const void*>(&tmK);
+          tma_load_4d(sKV + s * C::kKVBytes, map, bar_kv_full(s), 0, (i >> 1) * kQ4BN, h, b,
+                      pol_kv);
+          ++issued;
+        }
+        if (!kv_ok) break;
+        if (p.unit_ctr == nullptr) {
+          unit = p.total_units;
+        } else {
+          const unsigned int nx = gridDim.x + atomicAdd(p.unit_ctr, 1u);
+          unit = nx < static_cast<unsigned int>(p.total_units) ? static_cast<int>(nx)
+                                                               : p.total_units;
+        }
       }
       if (*abort_flag) {
-        drain_wait(bar_q, 0);
+        if (uc > 0) drain_wait(bar_q, (uc - 1) & 1);
         for (int i = max(0, issued - C::kStages); i < issued; ++i)
           drain_wait(bar_kv_full(i % C::kStages), (i / C::kStages) & 1);
       }
@@ -826,24 +999,38 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
     if (elect_one()) {
       constexpr uint32_t kIdQK = idesc_bf16_f32(kBM, kQ4BN, false, false);
       constexpr uint32_t kIdPV = idesc_bf16_f32(kBM, D, false, true);
-      bool ok = mbar_wait(bar_q, 0, abort_flag, p.status);
+      bool ok = true;
+      int it = 0;                     // K/V blocks consumed, over all units
+      int pb[kNT] = {0, 0, 0, 0};     // blocks of tile t in earlier units (P phases)
+      for (int uc = 0; ok; ++uc) {
+      const int us = uc & 1;
+      if (!mbar_wait(bar_unit_full(us), (uc >> 1) & 1, abort_flag, p.status)) break;
+      const int unit = unit_slot[us];
+      mbar_arrive(bar_unit_empty(us));
+      if (unit < 0) break;
+      int b, h, q0, nt[kNT];
+      decode_unit_q4<CAUSAL>(p, unit, b, h, q0, nt);
+      int n = 0;
+#pragma unroll
+      for (int t = 0; t < kNT; ++t) n = max(n, nt[t]);
+      if (!mbar_wait(bar_q, uc & 1, abort_flag, p.status)) break;
       tc_fence_after();
       int vslot = 0;
       for (int j = 0; ok && j <= n; ++j) {
         int kslot = 0;
         if (j < n) {
-          const int i = 2 * j;
-          kslot = i % C::kStages;
-          if (!mbar_wait(bar_kv_full(kslot), (i / C::kStages) & 1, abort_flag, p.status)) {
+          kslot = it % C::kStages;
+          if (!mbar_wait(bar_kv_full(kslot), (it / C::kStages) & 1, abort_flag, p.status)) {
             ok = false;
             break;
           }
+          ++it;
           tc_fence_after();
         }
 #pragma unroll
         for (int t = 0; t < kNT; ++t) {
           if (j >= 1 && j - 1 < nt[t]) {
-            if (!mbar_wait(bar_p_full(t), (j - 1) & 1, abort_flag, p.status)) {
+            if (!mbar_wait(bar_p_full(t), (pb[t] + j - 1) & 1, abort_flag, p.status)) {
               ok = false;
               break;
             }
@@ -871,14 +1058,18 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
         if (j >= 1) mma_commit(bar_kv_empty(vslot));
         if (j < n) {
           mma_commit(bar_kv_empty(kslot));
-          const int i = 2 * j + 1;
-          vslot = i % C::kStages;
-          if (!mbar_wait(bar_kv_full(vslot), (i / C::kStages) & 1, abort_flag, p.status)) {
+          if (j == n - 1) mma_commit(bar_q_empty);        // the unit's last S GEMMs
+          vslot = it % C::kStages;
+          if (!mbar_wait(bar_kv_full(vslot), (it / C::kStages) & 1, abort_flag, p.status)) {
             ok = false;
             break;
           }
+          ++it;
           tc_fence_after();
         }
+      }
+#pragma unroll
+      for (int t = 0; t < kNT; ++t) pb[t] += nt[t];
       }
       mma_commit(bar_drain);
       drain_wait(bar_drain, 0);
@@ -889,21 +1080,32 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
     const int t = warp >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
-    const int qi = q0 + t * kBM + row;
-    const int q_tile0 = q0 + t * kBM;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tS = tmem + lane_off + C::col_s(t);
     const uint32_t tO = tmem + lane_off + C::col_o(t);
     const float sl2 = p.scale_log2;
-    float m_ref = -INFINITY;
-    float l = 0.f;
     bool ok = true;
     auto wwait = [&](uint32_t bar, uint32_t parity) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status));
     };
+    int sb = 0;   // blocks of this tile in earlier units (S phases)
+    int ou = 0;   // earlier units in which this tile had work (O phases)
+    for (int uc = 0; ok; ++uc) {
+    const int us = uc & 1;
+    if (!wwait(bar_unit_full(us), (uc >> 1) & 1)) break;
+    const int unit = unit_slot[us];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_unit_empty(us));
+    if (unit < 0) break;
+    int b, h, q0, nt[kNT];
+    decode_unit_q4<CAUSAL>(p, unit, b, h, q0, nt);
+    const int qi = q0 + t * kBM + row;
+    const int q_tile0 = q0 + t * kBM;
+    float m_ref = -INFINITY;
+    float l = 0.f;
     const int my_nt = nt[t];
     for (int j = 0; j < my_nt; ++j) {
-      if (!wwait(bar_s_full(t), j & 1)) {
+      if (!wwait(bar_s_full(t), (sb + j) & 1)) {
         ok = false;
         break;
       }
@@ -989,7 +1191,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
       f2_unpack(rs2[1], b0, b1);
       l += (a0 + a1) + (b0 + b1);
     }
-    if (ok && my_nt > 0 && wwait(bar_o_full(t), 0)) {
+    if (ok && my_nt > 0 && wwait(bar_o_full(t), ou & 1)) {
       tc_fence_after();
       const float inv_l = 1.f / l;
       const int64_t orow_off = static_cast<int64_t>(b) * p.o_sb +
@@ -1023,6 +1225,9 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
         }
       }
     }
+    if (my_nt > 0) ++ou;
+    sb += my_nt;
+    }
   }
 
   tc_fence_before();
@@ -1030,6 +1235,13 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
   if (warp == 17) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0 && p.unit_ctr != nullptr) {
+    __threadfence();
+    if (atomicAdd(p.unit_ctr + 1, 1u) == gridDim.x - 1) {
+      atomicExch(p.unit_ctr, 0u);
+      atomicExch(p.unit_ctr + 1, 0u);
+    }
   }
 }
 
@@ -1057,6 +1269,35 @@ int launch_attn_q4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
 namespace fa {
 namespace {
 unsigned long long* g_trace_buffer = nullptr;
+std::mutex g_ctr_mu;
+unsigned int* g_ctr_base[64] = {};
+int g_sm_count[64] = {};
+std::atomic<unsigned int> g_ctr_next{0};
+
+// Per device: the SM count and the counter pair of the next persistent
+// launch.  A pair is reused after kUnitCtrSlots further launches; each launch
+// leaves its pair at zero when its last CTA exits, and launches in one stream
+// run in order, so a pair is never shared by two running launches unless
+// kUnitCtrSlots launches were issued in between while the first still ran.
+int persistent_setup(int dev, int* sms, unsigned int** ctr) {
+  if (dev < 0 || dev >= 64) return FA_ERR_DEVICE;
+  {
+    std::lock_guard<std::mutex> lk(g_ctr_mu);
+    if (g_ctr_base[dev] == nullptr) {
+      void* a = nullptr;
+      int n = 0;
+      if (cudaGetSymbolAddress(&a, g_attn_unit_ctr) != cudaSuccess) return FA_ERR_CUDA;
+      if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+          n <= 0)
+        return FA_ERR_CUDA;
+      g_ctr_base[dev] = static_cast<unsigned int*>(a);
+      g_sm_count[dev] = n;
+    }
+  }
+  *sms = g_sm_count[dev];
+  *ctr = g_ctr_base[dev] + 2 * (g_ctr_next.fetch_add(1) % kUnitCtrSlots);
+  return FA_OK;
+}
 }
 }  // namespace fa
 
@@ -1115,7 +1356,18 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
   prm.status = device_status_ptr();
   prm.trace = g_trace_buffer;
   if (prm.status == nullptr) return FA_ERR_CUDA;
-  const int grid = static_cast<int>(static_cast<int64_t>(B) * H * prm.n_units_per_head);
+  int grid = static_cast<int>(static_cast<int64_t>(B) * H * prm.n_units_per_head);
+  prm.total_units = grid;
+  prm.unit_ctr = nullptr;
+  if (FA_ATTN_PERSIST && (q4 || FA_ATTN_PINGPONG_D128 == 0)) {
+    int sms = 0;
+    unsigned int* ctr = nullptr;
+    if ((rc = persistent_setup(dev, &sms, &ctr)) != FA_OK) return rc;
+    if (grid > sms) {
+      prm.unit_ctr = ctr;
+      grid = sms;
+    }
+  }
   if (q4) {
     if (out_f32)
       return causal ? launch_attn_q4<true, true>(mq, mk, mv, prm, grid, stream)

@@ -28,6 +28,12 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
   return t;
 }
 
+__device__ __forceinline__ uint32_t smid() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %smid;" : "=r"(r));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -279,3 +279,56 @@ def test_attention_random_shapes_and_layouts(B, H, S, D, causal, layout):
     torch.cuda.synchronize()
     ref = oracle.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), causal=causal)
     assert_close(out.float().cpu().numpy(), ref, what=f"{layout} B{B} H{H} S{S} D{D} c={causal}")
+
+
+def _units(B, H, S, D):
+    rows = 512 if D == 64 else 256      # query rows per work unit
+    return B * H * ((S + rows - 1) // rows)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_persistent_launch_matches_oracle(D, causal):
+    """More work units than SMs: the kernel runs persistent, one CTA per SM
+    taking units from a global counter.  Every head is checked."""
+    B, H, S = 1, 160, 384
+    assert _units(B, H, S, D) > torch.cuda.get_device_properties(0).multi_processor_count
+    q, k, v = (_rand((B, H, S, D), 70 + i) for i in range(3))
+    out = _run(q, k, v, causal)
+    ref = oracle.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                           causal=causal)
+    assert_close(out, ref, what=f"persistent H{H} S{S} D{D} causal={causal}")
+
+
+def test_persistent_counter_pairs_wrap_and_reset():
+    """1100 persistent launches use every one of the 1024 counter pairs and
+    wrap around, so each pair must be left at zero by the launch before."""
+    q, k, v = (_rand((1, 160, 256, 128), 80 + i).to(DEV) for i in range(3))
+    first = attention(q, k, v, causal=True)
+    out = torch.empty_like(first)
+    for _ in range(1100):
+        attention(q, k, v, causal=True, out=out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, first)
+    assert device_status() == 0
+
+
+def test_persistent_launches_on_two_streams():
+    """Persistent launches in flight on two streams at once take different
+    counter pairs; each stream's results equal its single-launch output."""
+    ins = [[_rand((1, 160, 512, 128), 90 + 3 * s + i).to(DEV) for i in range(3)]
+           for s in range(2)]
+    want = [attention(*x, causal=bool(s)) for s, x in enumerate(ins)]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [torch.empty_like(w) for w in want]
+    bad = [0, 0]
+    for _ in range(40):
+        for s in range(2):
+            with torch.cuda.stream(streams[s]):
+                attention(*ins[s], causal=bool(s), out=outs[s])
+        for s in range(2):
+            streams[s].synchronize()
+            bad[s] += int(not torch.equal(outs[s], want[s]))
+    assert bad == [0, 0]
+    assert device_status() == 0
