@@ -209,9 +209,11 @@ struct AttnParams {
 
 // Optional timeline instrumentation (compiled out unless FA_ATTN_TRACE):
 // clock64() stamps per CTA for the first kTraceCtas CTAs, slot layout
-// [cta][iteration j][event], events 6t+0..6t+5 softmax tile t (wait start,
-// S ready, row max done, exp turn acquired, exps done, P stored + arrived),
-// 12+2t / 13+2t MMA tile t (P seen, S issued).
+// [cta][iteration j][event].  Two-tile kernel: events 6t+0..6t+5 softmax tile
+// t (wait start, S ready, row max done, exp turn acquired, exps done, P stored
+// + arrived), 12+2t / 13+2t MMA tile t (P seen, S issued).  Four-tile kernel:
+// events 4t+0..4t+3 softmax tile t (wait start, S ready, row max done, P
+// stored + arrived).  Later units of a persistent CTA overwrite earlier ones.
 // After those stamps, a per-unit record for the first kCtaTraceMax work units
 // (256 query rows of one head): [SM id, start, first S seen by tile 0, last O
 // ready, end, key blocks], the times from the global nanosecond timer so that
@@ -1105,11 +1107,13 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
     float l = 0.f;
     const int my_nt = nt[t];
     for (int j = 0; j < my_nt; ++j) {
+      if (lane == 0 && wq == 0) FA_TRACE(j, 4 * t + 0);
       if (!wwait(bar_s_full(t), (sb + j) & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      if (lane == 0 && wq == 0) FA_TRACE(j, 4 * t + 1);
       const int k0 = j * kQ4BN;
       const bool need_mask = (k0 + kQ4BN > p.S) || (CAUSAL && (k0 + kQ4BN - 1 > q_tile0));
       const int lim = CAUSAL ? min(qi + 1, p.S) : p.S;
@@ -1149,6 +1153,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
         l *= alpha;
         m_ref = m_use;
       }
+      if (lane == 0 && wq == 0) FA_TRACE(j, 4 * t + 2);
       const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
       const uint64_t sl2x2 = f2_pack(sl2, sl2);
       const uint64_t negm2 = f2_pack(neg_m, neg_m);
@@ -1186,6 +1191,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_p_full(t));
+      if (lane == 0 && wq == 0) FA_TRACE(j, 4 * t + 3);
       float a0, a1, b0, b1;
       f2_unpack(rs2[0], a0, a1);
       f2_unpack(rs2[1], b0, b1);
