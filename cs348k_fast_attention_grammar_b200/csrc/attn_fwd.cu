@@ -59,7 +59,7 @@ constexpr float kRescaleThreshold = 8.0f;
 #define FA_ATTN_EMU_MOD_D64 4
 #endif
 #ifndef FA_ATTN_EMU_MOD_D128
-#define FA_ATTN_EMU_MOD_D128 0
+#define FA_ATTN_EMU_MOD_D128 4
 #endif
 // 1 = pack probabilities to bf16 with integer ops (round half up), 0 = cvt.
 #ifndef FA_ATTN_PACK_ALU
