@@ -37,14 +37,21 @@ constexpr int kGBarOff = kGStages * kStageBytes;
 constexpr int kGNumBars = 2 * kGStages + 4 + 1;     // full, empty, acc_full[2], acc_empty[2], drain
 constexpr int kGMiscOff = kGBarOff + kGNumBars * 8;
 constexpr int kGSmemBytes = kGMiscOff + 16 + 1024;
+// Tile raster: bands of group_m M-tiles, M fastest inside a band, so the
+// band's rows of A stay in L2 while B streams past once per band.  The host
+// takes the largest power of two (up to 64) whose band of A fits in
+// FA_GEMM_BAND_MIB; FA_GEMM_GROUP_M > 0 forces a fixed band height instead.
 #ifndef FA_GEMM_GROUP_M
-#define FA_GEMM_GROUP_M 8
+#define FA_GEMM_GROUP_M 0
 #endif
-constexpr int kGroupM = FA_GEMM_GROUP_M;            // tile raster: M-tiles per band
+#ifndef FA_GEMM_BAND_MIB
+#define FA_GEMM_BAND_MIB 32
+#endif
 
 struct GemmParams {
   int M, N, K;
   int tiles_m, tiles_n, num_tiles;
+  int group_m;                // M-tiles per raster band
   int act;
   __nv_bfloat16* c;
   int64_t ldc;
@@ -61,10 +68,10 @@ __device__ __forceinline__ void gemm_drain_wait(uint32_t bar, uint32_t parity) {
 }
 
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& tm, int& tn) {
-  const int per_group = kGroupM * p.tiles_n;
+  const int per_group = p.group_m * p.tiles_n;
   const int g = tile / per_group;
-  const int first_m = g * kGroupM;
-  const int gm = min(p.tiles_m - first_m, kGroupM);
+  const int first_m = g * p.group_m;
+  const int gm = min(p.tiles_m - first_m, p.group_m);
   const int r = tile - g * per_group;
   tm = first_m + r % gm;
   tn = r / gm;
@@ -283,6 +290,15 @@ int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int6
   p.tiles_m = (M + kGBM - 1) / kGBM;
   p.tiles_n = (N + kGBN - 1) / kGBN;
   p.num_tiles = p.tiles_m * p.tiles_n;
+  if (FA_GEMM_GROUP_M > 0) {
+    p.group_m = FA_GEMM_GROUP_M;
+  } else {
+    const int64_t band_rows_bytes = static_cast<int64_t>(kGBM) * K * 2;   // one M-tile of A
+    p.group_m = 1;
+    while (p.group_m < 64 &&
+           2 * p.group_m * band_rows_bytes <= (static_cast<int64_t>(FA_GEMM_BAND_MIB) << 20))
+      p.group_m *= 2;
+  }
   p.act = act;
   p.c = static_cast<__nv_bfloat16*>(c);
   p.ldc = ldc;
