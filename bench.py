@@ -18,6 +18,7 @@ over ranks.  Rank 0 prints one JSON line.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -30,7 +31,6 @@ from datetime import timedelta
 ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
-
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
@@ -180,6 +180,22 @@ def timed_loop(fn, steps: int, world: int, device) -> float:
     return ms
 
 
+@contextlib.contextmanager
+def stdout_to_stderr():
+    """Point file descriptor 1 at stderr for the block: NCCL prints its
+    version banner on stdout when a communicator is created, and stdout
+    carries the one JSON line."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    try:
+        os.dup2(2, 1)
+        yield
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def host_cores() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -320,7 +336,9 @@ def main(argv=None):
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        with stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+            dist.barrier()
 
     import cs348k_fast_attention_grammar_b200 as fab
     fab.load()
