@@ -205,6 +205,9 @@ struct AttnParams {
   // Null: one unit per CTA (grid = total_units).
   int total_units;
   unsigned int* unit_ctr;
+  // 128-row Q tiles per work unit: the kernel's full width (2 or 4), or
+  // fewer for small problems so that more SMs get a unit.
+  int tiles_per_unit;
 };
 
 // Optional timeline instrumentation (compiled out unless FA_ATTN_TRACE):
@@ -249,8 +252,8 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
-// Work unit u of the two-tile kernel: 256 query rows (two 128-row tiles) of
-// one (batch, head) pair.  Pairs are taken in consecutive groups of
+// Work unit u of the two-tile kernel: tiles_per_unit (2, or 1 for small
+// problems) 128-row Q tiles of one (batch, head) pair.  Pairs are taken in consecutive groups of
 // group_q + 1 (the first group_r groups) or group_q pairs, so the K/V of a
 // group stay resident in L2.  Inside a group the units run
 // query-position-major, and for causal attention the longest (last) query
@@ -280,11 +283,11 @@ __device__ __forceinline__ void decode_unit(const AttnParams& p, int unit, int& 
   if (CAUSAL) qu = p.n_units_per_head - 1 - qu;
   b = bh / p.H;
   h = bh - b * p.H;
-  q0 = qu * 2 * kBM;
+  q0 = qu * p.tiles_per_unit * kBM;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     const int qs = q0 + t * kBM;
-    if (qs >= p.S) nt[t] = 0;
+    if (t >= p.tiles_per_unit || qs >= p.S) nt[t] = 0;
     else if (CAUSAL) nt[t] = min(p.nkv, qs / kBN + 1);
     else nt[t] = p.nkv;
   }
@@ -379,6 +382,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
+      // Launched as a programmatic dependent of the staging kernel, Q/K/V are
+      // complete only after this wait (a no-op for ordinary launches).  Every
+      // other role consumes what these loads bring, so it orders them too.
+      grid_dependency_wait();
       int issued = 0;     // K/V tiles issued, over all units (ring position)
       int uc = 0;         // units published
       int unit = blockIdx.x;
@@ -398,13 +405,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The Q tiles are free once the previous unit's last S GEMMs are done;
         // this unit's Q and first K/V tiles land while that unit finishes.
         if (uc > 0 && !mbar_wait(bar_q_empty, (uc - 1) & 1, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(bar_q, 2 * C::kTileBytes);
+        mbar_arrive_expect_tx(bar_q, (nt[1] > 0 ? 2 : 1) * C::kTileBytes);
 #pragma unroll
         for (int t = 0; t < 2; ++t)
+          if (nt[t] > 0)
 #pragma unroll
-          for (int dk = 0; dk < D / 64; ++dk)
-            tma_load_4d(sQ + t * C::kTileBytes + dk * 16384, &tmQ, bar_q, dk * 64,
-                        q0 + t * kBM, h, b, pol_q);
+            for (int dk = 0; dk < D / 64; ++dk)
+              tma_load_4d(sQ + t * C::kTileBytes + dk * 16384, &tmQ, bar_q, dk * 64,
+                          q0 + t * kBM, h, b, pol_q);
         ++uc;
         bool kv_ok = true;
         for (int i = 0; i < 2 * n; ++i) {
@@ -780,9 +788,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Launch; with pdl, as a programmatic dependent of the previous kernel in the
+// stream (it may start while that kernel runs; its producer waits for it).
+template <typename Kern>
+int launch_maybe_pdl(Kern kern, int grid, int threads, int smem, cudaStream_t stream, bool pdl,
+                     const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                     const AttnParams& prm) {
+  if (!pdl) {
+    kern<<<grid, threads, smem, stream>>>(mq, mk, mv, prm);
+    return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, prm) == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
+
 template <int D, bool CAUSAL, bool OUT_F32>
 int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                const AttnParams& prm, int grid, cudaStream_t stream) {
+                const AttnParams& prm, int grid, cudaStream_t stream, bool pdl) {
   using C = AttnCfg<D>;
   auto kern = attn_fwd_kernel<D, CAUSAL, OUT_F32>;
   static bool attr_set[64] = {};
@@ -794,8 +825,7 @@ int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
     if (rc != FA_OK) return rc;
     attr_set[dev] = true;
   }
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(mq, mk, mv, prm);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  return launch_maybe_pdl(kern, grid, kThreads, C::kSmemBytes, stream, pdl, mq, mk, mv, prm);
 }
 
 // D = 64 kernel: four 128-row Q tiles per CTA (512 query rows) and 64-key
@@ -825,9 +855,9 @@ struct AttnQ4Cfg {
   __device__ static constexpr uint32_t col_o(int t) { return 256u + 64u * t; }
 };
 
-// Work unit u of the four-tile kernel: 512 query rows (four 128-row tiles)
-// of one (batch, head) pair, ordered as decode_unit orders the two-tile
-// kernel's units.  nt[t] = 64-key blocks of tile t (0 past S).
+// Work unit u of the four-tile kernel: tiles_per_unit (4, or 2 or 1 for
+// small problems) 128-row Q tiles of one (batch, head) pair, ordered as
+// decode_unit orders the two-tile kernel's units.  nt[t] = 64-key blocks of tile t (0 past S).
 template <bool CAUSAL>
 __device__ __forceinline__ void decode_unit_q4(const AttnParams& p, int unit, int& b, int& h,
                                                int& q0, int nt[4]) {
@@ -852,11 +882,11 @@ __device__ __forceinline__ void decode_unit_q4(const AttnParams& p, int unit, in
   if (CAUSAL) qu = p.n_units_per_head - 1 - qu;
   b = bh / p.H;
   h = bh - b * p.H;
-  q0 = qu * 4 * kBM;
+  q0 = qu * p.tiles_per_unit * kBM;
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
     const int qs = q0 + t * kBM;
-    if (qs >= p.S) nt[t] = 0;
+    if (t >= p.tiles_per_unit || qs >= p.S) nt[t] = 0;
     else if (CAUSAL) nt[t] = min(p.nkv, (qs + kBM - 1) / kQ4BN + 1);
     else nt[t] = p.nkv;
   }
@@ -937,6 +967,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
     if (elect_one()) {
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
+      grid_dependency_wait();   // see attn_fwd_kernel
       int issued = 0;     // K/V blocks issued, over all units (ring position)
       int uc = 0;         // units published
       int unit = blockIdx.x;
@@ -1253,7 +1284,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
 
 template <bool CAUSAL, bool OUT_F32>
 int launch_attn_q4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                   const AttnParams& prm, int grid, cudaStream_t stream) {
+                   const AttnParams& prm, int grid, cudaStream_t stream, bool pdl) {
   using C = AttnQ4Cfg;
   auto kern = attn_fwd_q4_kernel<CAUSAL, OUT_F32>;
   static bool attr_set[64] = {};
@@ -1265,8 +1296,7 @@ int launch_attn_q4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
     if (rc != FA_OK) return rc;
     attr_set[dev] = true;
   }
-  kern<<<grid, kQ4Threads, C::kSmemBytes, stream>>>(mq, mk, mv, prm);
-  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  return launch_maybe_pdl(kern, grid, kQ4Threads, C::kSmemBytes, stream, pdl, mq, mk, mv, prm);
 }
 
 }  // namespace
@@ -1321,14 +1351,23 @@ namespace {
 // Shared host path of fa_attn_fwd / fa_attn_fwd_f32 (arguments already
 // validated): tensor maps, scheduling groups, launch.
 int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D,
-             const int64_t* st, int causal, float scale, bool out_f32, cudaStream_t stream) {
+             const int64_t* st, int causal, float scale, bool out_f32, cudaStream_t stream,
+             bool pdl = false) {
   int dev = 0;
   int rc = prepare_device(nullptr, 0, &dev);
   if (rc != FA_OK) return rc;
   // D = 64: four-tile kernel with 64-key blocks; D = 128: two-tile kernel.
   const bool q4 = (D == 64);
   const int kv_rows = q4 ? kQ4BN : kBN;                  // keys per K/V block
-  const int unit_rows = q4 ? 4 * kBM : 2 * kBM;          // query rows per CTA
+  // Tiles per work unit: the kernel's width, halved while at most half the
+  // SMs would get a unit (small problems spread over more SMs; a unit's
+  // tiles share its K/V loads, so wide units stay where SMs are all busy).
+  int sms = 0, tpu = q4 ? 4 : 2;
+  unsigned int* ctr = nullptr;
+  if ((rc = persistent_setup(dev, &sms, &ctr)) != FA_OK) return rc;
+  while (tpu > 1 && 2 * static_cast<int64_t>(B) * H * ((S + tpu * kBM - 1) / (tpu * kBM)) <= sms)
+    tpu /= 2;
+  const int unit_rows = tpu * kBM;                         // query rows per unit
   CUtensorMap mq, mk, mv;
   if ((rc = make_tmap_bhsd(&mq, q, B, H, S, D, st[0], st[1], st[2], kBM)) != FA_OK) return rc;
   if ((rc = make_tmap_bhsd(&mk, k, B, H, S, D, st[4], st[5], st[6], kv_rows)) != FA_OK) return rc;
@@ -1365,27 +1404,23 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
   int grid = static_cast<int>(static_cast<int64_t>(B) * H * prm.n_units_per_head);
   prm.total_units = grid;
   prm.unit_ctr = nullptr;
-  if (FA_ATTN_PERSIST && (q4 || FA_ATTN_PINGPONG_D128 == 0)) {
-    int sms = 0;
-    unsigned int* ctr = nullptr;
-    if ((rc = persistent_setup(dev, &sms, &ctr)) != FA_OK) return rc;
-    if (grid > sms) {
-      prm.unit_ctr = ctr;
-      grid = sms;
-    }
+  prm.tiles_per_unit = tpu;
+  if (FA_ATTN_PERSIST && (q4 || FA_ATTN_PINGPONG_D128 == 0) && grid > sms) {
+    prm.unit_ctr = ctr;
+    grid = sms;
   }
   if (q4) {
     if (out_f32)
-      return causal ? launch_attn_q4<true, true>(mq, mk, mv, prm, grid, stream)
-                    : launch_attn_q4<false, true>(mq, mk, mv, prm, grid, stream);
-    return causal ? launch_attn_q4<true, false>(mq, mk, mv, prm, grid, stream)
-                  : launch_attn_q4<false, false>(mq, mk, mv, prm, grid, stream);
+      return causal ? launch_attn_q4<true, true>(mq, mk, mv, prm, grid, stream, pdl)
+                    : launch_attn_q4<false, true>(mq, mk, mv, prm, grid, stream, pdl);
+    return causal ? launch_attn_q4<true, false>(mq, mk, mv, prm, grid, stream, pdl)
+                  : launch_attn_q4<false, false>(mq, mk, mv, prm, grid, stream, pdl);
   }
   if (out_f32)
-    return causal ? launch_attn<128, true, true>(mq, mk, mv, prm, grid, stream)
-                  : launch_attn<128, false, true>(mq, mk, mv, prm, grid, stream);
-  return causal ? launch_attn<128, true, false>(mq, mk, mv, prm, grid, stream)
-                : launch_attn<128, false, false>(mq, mk, mv, prm, grid, stream);
+    return causal ? launch_attn<128, true, true>(mq, mk, mv, prm, grid, stream, pdl)
+                  : launch_attn<128, false, true>(mq, mk, mv, prm, grid, stream, pdl);
+  return causal ? launch_attn<128, true, false>(mq, mk, mv, prm, grid, stream, pdl)
+                : launch_attn<128, false, false>(mq, mk, mv, prm, grid, stream, pdl);
 }
 
 // fp32 -> bf16 staging of the reference's 2-D operands into the workspace
@@ -1397,6 +1432,9 @@ __global__ void __launch_bounds__(256)
                      const float* __restrict__ v, __nv_bfloat16* __restrict__ ws, int N, int D,
                      int k_transposed) {
   __shared__ float tile[32][33];
+  // The attention kernel may start its set-up now; its loads wait for this
+  // grid to complete.
+  grid_dependents_launch();
   const int z = blockIdx.z;
   const float* src = (z == 0) ? q : (z == 1) ? k : v;
   __nv_bfloat16* dst = ws + static_cast<int64_t>(z) * N * D;
@@ -1438,7 +1476,7 @@ extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o,
   if (!q || !k || !v || !o || !st) return FA_ERR_NULL;
   if (B <= 0 || H <= 0 || S <= 0) return FA_ERR_SHAPE;
   if (D != 64 && D != 128) return FA_ERR_HEAD_DIM;
-  const int64_t units = static_cast<int64_t>(B) * H * ((S + 2 * kBM - 1) / (2 * kBM));
+  const int64_t units = static_cast<int64_t>(B) * H * ((S + kBM - 1) / kBM);
   if (units > 0x7fffffffLL) return FA_ERR_SHAPE;
   for (int t = 0; t < 4; ++t) {
     if (st[4 * t + 3] != 1) return FA_ERR_STRIDE;
@@ -1475,5 +1513,6 @@ extern "C" int fa_attn_fwd_f32(const void* q, const void* k, const void* v, void
   if (cudaGetLastError() != cudaSuccess) return FA_ERR_LAUNCH;
   const int64_t nd = static_cast<int64_t>(N) * D;
   const int64_t st[16] = {nd, nd, D, 1, nd, nd, D, 1, nd, nd, D, 1, nd, nd, D, 1};
-  return run_attn(wb, wb + nd, wb + 2 * nd, o, 1, 1, N, D, st, causal, scale, true, s);
+  return run_attn(wb, wb + nd, wb + 2 * nd, o, 1, 1, N, D, st, causal, scale, true, s,
+                  /*pdl=*/true);
 }

@@ -28,6 +28,16 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
   return t;
 }
 
+// Programmatic dependent launch: the dependent grid waits here until the
+// grids it depends on have completed and their writes are visible (returns at
+// once for ordinary launches); a prerequisite grid lets its dependents launch.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smid() {
   uint32_t r;
   asm volatile("mov.u32 %0, %smid;" : "=r"(r));

@@ -37,8 +37,34 @@ from . import _lib
 _BF16 = torch.bfloat16
 
 
+# torch's raw current-stream accessor (the one its compiled kernels use) is
+# ~10x cheaper than torch.cuda.current_stream(); small calls are host bound.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream_ptr(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
+
+
+# bf16 staging workspaces of attention_f32 up to this size are kept per
+# (device, stream) and reused; work on one stream is ordered, so a reused
+# workspace is never written while an earlier call still reads it.
+_WS_CACHE_MAX_ELEMS = 8 << 20
+_ws_cache: dict = {}
+
+
+def _staging_workspace(n_elems: int, device: torch.device, stream: int) -> torch.Tensor:
+    if n_elems > _WS_CACHE_MAX_ELEMS:
+        return torch.empty(n_elems, dtype=_BF16, device=device)
+    key = (device.index, stream)
+    ws = _ws_cache.get(key)
+    if ws is None or ws.numel() < n_elems:
+        ws = torch.empty(max(n_elems, 1 << 16), dtype=_BF16, device=device)
+        _ws_cache[key] = ws
+    return ws
 
 
 class _on_device:
@@ -137,14 +163,15 @@ def attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
         raise ValueError("q, k, v must be on the same device")
     if out is None:
         out = torch.empty((N, D), dtype=torch.float32, device=q.device)
-    ws = torch.empty(3 * N * D, dtype=_BF16, device=q.device)
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     lib = _lib.load()
     with _on_device(q.device):
+        stream = _stream_ptr(q.device)
+        ws = _staging_workspace(3 * N * D, q.device, stream)
         rc = lib.fa_attn_fwd_f32(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                                  ws.data_ptr(), N, D, int(bool(k_transposed)),
-                                 int(bool(causal)), float(scale), _stream_ptr(q.device))
+                                 int(bool(causal)), float(scale), stream)
     _lib.check(rc, "fa_attn_fwd_f32")
     return out
 
