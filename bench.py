@@ -496,23 +496,26 @@ def bench_ref512(args, fab, device, world, rank):
     ins = [torch.randn(*dims, generator=g, device=device, dtype=torch.float32)
            for _name, dims in kernel_module.KERNEL_META["inputs"]]
     step = lambda: kernel_module.fn(*ins)  # noqa: E731
-    for _ in range(max(args.warmup, 0)):
+    # One call is ~20 us of host and GPU work: time at least 1000 of them so
+    # the loop's fixed cost does not weigh on the per-call figure.
+    warmup, steps = max(args.warmup, 200), max(args.steps, 1000)
+    for _ in range(warmup):
         step()
     with ClockSampler(local_index(device)) as clk:
-        ms = timed_loop(step, args.steps, world, device)
+        ms = timed_loop(step, steps, world, device)
     value = REF512_FLOPS * world / (ms * 1e-3) / 1e12
     # Like-for-like on the same GPU: the reference's flash-attn2-sota.py call,
     # torch SDPA on [1, 1, 512, 64] fp32 (its fn(K, Q, V)), timed the same way.
     KT, Q, V = ins
     k4, q4, v4 = (t.reshape(1, 1, 512, 64) for t in (KT.t().contiguous(), Q, V))
     sdpa = lambda: torch.nn.functional.scaled_dot_product_attention(q4, k4, v4)  # noqa: E731
-    for _ in range(max(args.warmup, 0)):
+    for _ in range(warmup):
         sdpa()
-    ms_sdpa = timed_loop(sdpa, args.steps, world, device)
+    ms_sdpa = timed_loop(sdpa, steps, world, device)
     peaks = load_peaks()
     return {"metric": "reference kernel-module attention TFLOP/s (program_flops, N=512 d=64)",
-            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": value / REF512_PUBLISHED_TFLOPS,
             "vs_baseline_note": "published 0.646 TFLOP/s is the reference's best searched "
                                 "kernel on an NVIDIA L4 (results/attn-full.json)",
@@ -525,7 +528,7 @@ def bench_ref512(args, fab, device, world, rank):
                               "unit": "TFLOP/s", "ms_per_call": ms_sdpa,
                               "what": "torch scaled_dot_product_attention fp32 [1,1,512,64] "
                                       "(flash-attn2-sota.py's call) on this GPU"},
-            "gpu_launches": 2 * args.steps, "clocks": clk.summary(), "cpu_baseline": None,
+            "gpu_launches": 2 * steps, "clocks": clk.summary(), "cpu_baseline": None,
             "e2e": None}
 
 

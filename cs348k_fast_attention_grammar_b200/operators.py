@@ -62,6 +62,10 @@ def _staging_workspace(n_elems: int, device: torch.device, stream: int) -> torch
     key = (device.index, stream)
     ws = _ws_cache.get(key)
     if ws is None or ws.numel() < n_elems:
+        if ws is None and len(_ws_cache) >= 16:
+            # Many streams: drop the cache (torch's allocator reuses a freed
+            # block only for work on the stream it was allocated on).
+            _ws_cache.clear()
         ws = torch.empty(max(n_elems, 1 << 16), dtype=_BF16, device=device)
         _ws_cache[key] = ws
     return ws
