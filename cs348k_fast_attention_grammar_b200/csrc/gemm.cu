@@ -21,6 +21,7 @@
 #include "fa_internal.h"
 #include "sm100_ptx.cuh"
 #include "sm100_tmem_wide.cuh"
+#include "sm100_2sm.cuh"
 
 namespace fa {
 namespace {
@@ -85,6 +86,40 @@ __device__ __forceinline__ float apply_act(float x, int act) {
     return fmaf(hx, tanh_approx(u), hx);
   }
   return x;
+}
+
+// Epilogue of 32 accumulator columns of one row: activation, optional bf16
+// residual (added in fp32), bf16 pack, 16-byte stores; rows >= M and columns
+// >= N (N is a multiple of 32) are skipped.
+__device__ __forceinline__ void store_chunk(const GemmParams& p, int row, int col,
+                                            const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) v[e] = apply_act(__uint_as_float(r[e]), p.act);
+  const bool in = row < p.M && col < p.N;
+  if (p.res != nullptr && in) {
+    const uint4* rs = reinterpret_cast<const uint4*>(p.res + static_cast<int64_t>(row) * p.ldr + col);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 u = __ldg(rs + q);
+      const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[8 * q + 2 * e] += __uint_as_float(ws[e] << 16);
+        v[8 * q + 2 * e + 1] += __uint_as_float(ws[e] & 0xffff0000u);
+      }
+    }
+  }
+  uint32_t w[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+  if (in) {
+    uint4* dst = reinterpret_cast<uint4*>(p.c + static_cast<int64_t>(row) * p.ldc + col);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+    dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+  }
 }
 
 __global__ void __launch_bounds__(kGThreads, 1)
@@ -217,39 +252,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
         break;
       tc_fence_after();
       const int row = tm * kGBM + row_in_tile;
-      __nv_bfloat16* crow = p.c + static_cast<int64_t>(row) * p.ldc + tn * kGBN;
 #pragma unroll 1
       for (int c = 0; c < kGBN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32_wait(tmem + lane_off + 256u * acc + c * 32, r);
-        float v[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = apply_act(__uint_as_float(r[e]), p.act);
-        if (p.res != nullptr && row < p.M && tn * kGBN + c * 32 < p.N) {
-          // residual: 32 bf16 of the same row and columns, added in fp32
-          const uint4* rs = reinterpret_cast<const uint4*>(
-              p.res + static_cast<int64_t>(row) * p.ldr + tn * kGBN + c * 32);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 u = __ldg(rs + q);
-            const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              v[8 * q + 2 * e] += __uint_as_float(ws[e] << 16);
-              v[8 * q + 2 * e + 1] += __uint_as_float(ws[e] & 0xffff0000u);
-            }
-          }
-        }
-        uint32_t w[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
-        if (row < p.M && tn * kGBN + c * 32 < p.N) {
-          uint4* dst = reinterpret_cast<uint4*>(crow + c * 32);
-          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-          dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
-          dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
-        }
+        store_chunk(p, row, tn * kGBN + c * 32, r);
       }
       tc_fence_before();
       mbar_arrive(bar_acc_empty(acc));
@@ -264,8 +271,187 @@ __global__ void __launch_bounds__(kGThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Two-SM variant: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256).  CTA r of the pair loads rows
+// [128 r, 128 r + 128) of the A tile and columns [128 r, 128 r + 128) of the
+// B tile per 64-deep K step (32 KiB per CTA and stage), so each SM moves two
+// thirds of the one-SM kernel's L2 -> shared-memory bytes per FLOP.  Rank 0
+// expects both CTAs' bytes on its full barrier and issues the MMAs; its
+// commits arrive on the empty and accumulator barriers of both CTAs; each CTA
+// drains its own 128 TMEM lanes and reports to rank 0's accumulator-empty
+// barrier.
+// ---------------------------------------------------------------------------
+#ifndef FA_GEMM_2SM
+#define FA_GEMM_2SM 1
+#endif
+constexpr int kG2BM = 256;                          // tile rows (both CTAs)
+constexpr int kG2BN = 256;                          // tile columns (both CTAs)
+constexpr int kG2Stages = 6;
+constexpr int kG2ABytes = 128 * kGBK * 2;           // 16 KiB: this CTA's rows of A
+constexpr int kG2BBytes = kGBK * 128 * 2;           // 16 KiB: this CTA's columns of B
+constexpr int kG2StageBytes = kG2ABytes + kG2BBytes;
+constexpr int kG2BarOff = kG2Stages * kG2StageBytes;
+constexpr int kG2NumBars = 2 * kG2Stages + 4 + 1;  // full, empty, acc_full[2], acc_empty[2], drain
+constexpr int kG2MiscOff = kG2BarOff + kG2NumBars * 8;
+constexpr int kG2SmemBytes = kG2MiscOff + 16 + 1024;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
+    gemm_act_2sm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bars = base + kG2BarOff;
+  auto bar_full = [&](int s) { return bars + 8u * s; };
+  auto bar_empty = [&](int s) { return bars + 8u * (kG2Stages + s); };
+  auto bar_acc_full = [&](int a) { return bars + 8u * (2 * kG2Stages + a); };
+  auto bar_acc_empty = [&](int a) { return bars + 8u * (2 * kG2Stages + 2 + a); };
+  const uint32_t bar_drain = bars + 8u * (2 * kG2Stages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kG2MiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + kG2MiscOff + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nk = p.K / kGBK;
+  const uint32_t rank = cluster_ctarank();
+  const int first_tile = static_cast<int>(blockIdx.x >> 1);
+  const int tile_step = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kG2Stages; ++s) {
+      mbar_init(bar_full(s), 1);
+      mbar_init(bar_empty(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_acc_full(a), 1);
+      mbar_init(bar_acc_empty(a), 2 * 4);   // one lane of each epilogue warp, both CTAs
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_2sm(smem_u32(tmem_slot), 512);
+    tmem_relinquish_2sm();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  cluster_sync();     // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // =================== TMA producer (both CTAs) ===================
+    if (elect_one()) {
+      const uint64_t pol = l2_policy_evict_last();
+      int it = 0;
+      bool ok = true;
+      for (int tile = first_tile; ok && tile < p.num_tiles; tile += tile_step) {
+        int tm, tn;
+        tile_coords(p, tile, tm, tn);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kG2Stages;
+          const uint32_t ph = (it / kG2Stages) & 1;
+          if (!mbar_wait(bar_empty(s), ph ^ 1u, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + s * kG2StageBytes;
+          const uint32_t sb = sa + kG2ABytes;
+          if (rank == 0) mbar_arrive_expect_tx(bar_full(s), 2 * kG2StageBytes);
+          tma_load_2d_2sm(sa, &tmA, bar_full(s), kb * kGBK, tm * kG2BM + 128 * rank, pol);
+#pragma unroll
+          for (int a = 0; a < 2; ++a)
+            tma_load_2d_2sm(sb + a * 8192, &tmB, bar_full(s), tn * kG2BN + 128 * rank + a * 64,
+                            kb * kGBK, pol);
+        }
+      }
+      if (!ok && rank == 0) {
+        for (int i = max(0, it - kG2Stages); i < it; ++i)
+          gemm_drain_wait(bar_full(i % kG2Stages), (i / kG2Stages) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // =================== MMA issuer (rank 0) ===================
+    if (rank == 0 && elect_one()) {
+      constexpr uint32_t kId = idesc_bf16_f32(kG2BM, kG2BN, false, true);
+      int it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = first_tile; ok && tile < p.num_tiles; tile += tile_step, ++tcount) {
+        const int acc = tcount & 1;
+        const uint32_t use = static_cast<uint32_t>(tcount >> 1);
+        if (!mbar_wait(bar_acc_empty(acc), (use & 1u) ^ 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t dt = tmem + 256u * acc;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kG2Stages;
+          if (!mbar_wait(bar_full(s), (it / kG2Stages) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + s * kG2StageBytes;
+          const uint32_t sb = sa + kG2ABytes;
+#pragma unroll
+          for (int kk = 0; kk < kGBK / 16; ++kk) {
+            const uint64_t ad = sdesc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(sb + kk * 2048, 8192, 1024);
+            mma_ss_2sm(dt, ad, bd, kId, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit_2sm_mc(bar_empty(s), 0x3);
+        }
+        if (!ok) break;
+        mma_commit_2sm_mc(bar_acc_full(acc), 0x3);
+      }
+      mma_commit_2sm(bar_drain);
+      gemm_drain_wait(bar_drain, 0);
+    }
+    __syncwarp();
+  } else {
+    // =================== epilogue (warps 2..5, both CTAs) ===================
+    const int wq = warp & 3;
+    const int row_in_tile = 128 * static_cast<int>(rank) + wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    int tcount = 0;
+    for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++tcount) {
+      int tm, tn;
+      tile_coords(p, tile, tm, tn);
+      const int acc = tcount & 1;
+      const uint32_t use = static_cast<uint32_t>(tcount >> 1);
+      if (!__all_sync(0xffffffffu, mbar_wait(bar_acc_full(acc), use & 1u, abort_flag, p.status)))
+        break;
+      tc_fence_after();
+      const int row = tm * kG2BM + row_in_tile;
+#pragma unroll 1
+      for (int c = 0; c < kG2BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32_wait(tmem + lane_off + 256u * acc + c * 32, r);
+        store_chunk(p, row, tn * kG2BN + c * 32, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(bar_acc_empty(acc), 0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();     // neither CTA's barriers or TMEM are touched after this
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_2sm(tmem, 512);
+  }
+}
+
 int g_num_sms[64] = {};
 bool g_gemm_attr[64] = {};
+int g_clusters_2sm[64] = {};     // co-resident clusters of gemm_act_2sm_kernel
 
 int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int64_t lda,
                 int64_t ldb, int64_t ldc, int act, cudaStream_t stream,
@@ -287,13 +473,18 @@ int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int6
   p.M = M;
   p.N = N;
   p.K = K;
-  p.tiles_m = (M + kGBM - 1) / kGBM;
-  p.tiles_n = (N + kGBN - 1) / kGBN;
+  // Two-SM tiles (256 x 256 per SM pair) once there are enough of them to
+  // keep every pair busy; small problems keep the one-SM 128 x 256 tiles.
+  const bool two_sm = FA_GEMM_2SM && M >= 2048 && N >= 1024;
+  const int bm = two_sm ? kG2BM : kGBM;
+  const int bn = two_sm ? kG2BN : kGBN;
+  p.tiles_m = (M + bm - 1) / bm;
+  p.tiles_n = (N + bn - 1) / bn;
   p.num_tiles = p.tiles_m * p.tiles_n;
   if (FA_GEMM_GROUP_M > 0) {
     p.group_m = FA_GEMM_GROUP_M;
   } else {
-    const int64_t band_rows_bytes = static_cast<int64_t>(kGBM) * K * 2;   // one M-tile of A
+    const int64_t band_rows_bytes = static_cast<int64_t>(bm) * K * 2;   // one M-tile of A
     p.group_m = 1;
     while (p.group_m < 64 &&
            2 * p.group_m * band_rows_bytes <= (static_cast<int64_t>(FA_GEMM_BAND_MIB) << 20))
@@ -306,6 +497,25 @@ int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int6
   p.ldr = ldr;
   p.status = device_status_ptr();
   if (p.status == nullptr) return FA_ERR_CUDA;
+  if (two_sm) {
+    if (g_clusters_2sm[dev] == 0) {
+      if (cudaFuncSetAttribute(gemm_act_2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kG2SmemBytes) != cudaSuccess)
+        return FA_ERR_CUDA;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * 74);
+      cfg.blockDim = dim3(kGThreads);
+      cfg.dynamicSmemBytes = kG2SmemBytes;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_act_2sm_kernel, &cfg) != cudaSuccess || n <= 0)
+        n = (g_num_sms[dev] > 0 ? g_num_sms[dev] : 148) / 2;
+      cudaGetLastError();
+      g_clusters_2sm[dev] = n;
+    }
+    const int grid = 2 * min(p.num_tiles, g_clusters_2sm[dev]);
+    gemm_act_2sm_kernel<<<grid, kGThreads, kG2SmemBytes, stream>>>(ma, mb, p);
+    return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+  }
   const int grid = min(p.num_tiles, g_num_sms[dev] > 0 ? g_num_sms[dev] : 148);
   gemm_act_kernel<<<grid, kGThreads, kGSmemBytes, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
