@@ -27,11 +27,10 @@
 // 0-63, then 64-127), and O_t += P_t V starts on the first half while the
 // softmax computes the second.
 // This two-tile kernel serves D = 128; D = 64 runs attn_fwd_q4_kernel below
-// (four Q tiles per CTA over 64-key blocks).  The D = 64 branches of the
-// two-tile kernel (exp turns between the warpgroups, FMA-pipe exponentials)
-// remain compilable for comparison but are not dispatched.
+// (four Q tiles per CTA over 64-key blocks).
 // Scheduling: (batch, head) pairs in groups of <= 32 MiB of K/V (L2-resident),
-// causal units longest first within a group.
+// causal units longest first within a group; one CTA per SM takes work units
+// from a global counter once there are more units than SMs.
 // Online softmax (exp2 domain, log2(e) folded into the scale): the running
 // row maximum is only raised when a block's maximum exceeds it by more than
 // 8 (a factor 256), which keeps O_t rescales rare; the final O / l is exact
@@ -86,13 +85,6 @@ constexpr float kRescaleThreshold = 8.0f;
 // 1 = FMA-pipe exponentials computed two at a time (exp2_fma_x2).
 #ifndef FA_ATTN_EMU2
 #define FA_ATTN_EMU2 1
-#endif
-// 1 = the two softmax warpgroups take turns on their exp phases (per D).
-#ifndef FA_ATTN_PINGPONG_D64
-#define FA_ATTN_PINGPONG_D64 1
-#endif
-#ifndef FA_ATTN_PINGPONG_D128
-#define FA_ATTN_PINGPONG_D128 0
 #endif
 // 1 = move registers from the producer/MMA warpgroup (56 per thread) to the
 // two softmax warpgroups (224 per thread) with setmaxnreg.  The split adds up
@@ -177,8 +169,8 @@ struct AttnCfg {
   static constexpr int kKVOff = 2 * kTileBytes;
   static constexpr int kBarOff = kKVOff + kStages * kTileBytes;
   // q_full, kv_full[kStages], kv_empty[kStages], s_full[2], p_full[2],
-  // o_full[2], drain, turn[2], p_half[2], q_empty, unit_full[2], unit_empty[2]
-  static constexpr int kNumBars = 1 + 2 * kStages + 16;
+  // o_full[2], drain, p_half[2], q_empty, unit_full[2], unit_empty[2]
+  static constexpr int kNumBars = 1 + 2 * kStages + 14;
   // tmem base, abort flag, unit ring (2 ints)
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + alignment slack
@@ -213,7 +205,7 @@ struct AttnParams {
 // Optional timeline instrumentation (compiled out unless FA_ATTN_TRACE):
 // clock64() stamps per CTA for the first kTraceCtas CTAs, slot layout
 // [cta][iteration j][event].  Two-tile kernel: events 6t+0..6t+5 softmax tile
-// t (wait start, S ready, row max done, exp turn acquired, exps done, P stored
+// t (wait start, S ready, row max done, exps start, exps done, P stored
 // + arrived), 12+2t / 13+2t MMA tile t (P seen, S issued).  Four-tile kernel:
 // events 4t+0..4t+3 softmax tile t (wait start, S ready, row max done, P
 // stored + arrived).  Later units of a persistent CTA overwrite earlier ones.
@@ -315,21 +307,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar_p_full = [&](int t) { return bars + 8u * (3 + 2 * C::kStages + t); };
   auto bar_o_full = [&](int t) { return bars + 8u * (5 + 2 * C::kStages + t); };
   const uint32_t bar_drain = bars + 8u * (7 + 2 * C::kStages);
-  // turn[t] completes each time the other softmax warpgroup ends an exp phase.
-  auto bar_turn = [&](int t) { return bars + 8u * (8 + 2 * C::kStages + t); };
   // p_half[t] completes when the first 64 keys of P_t are in TMEM.
-  auto bar_p_half = [&](int t) { return bars + 8u * (10 + 2 * C::kStages + t); };
+  auto bar_p_half = [&](int t) { return bars + 8u * (8 + 2 * C::kStages + t); };
   // q_empty completes when a unit's last S GEMMs are done (the Q tiles are free).
-  const uint32_t bar_q_empty = bars + 8u * (12 + 2 * C::kStages);
+  const uint32_t bar_q_empty = bars + 8u * (10 + 2 * C::kStages);
   // Unit ring: the producer writes unit_slot[s] and arrives on unit_full[s];
   // the MMA thread and the eight softmax warps arrive on unit_empty[s] once
   // they have read it.  -1 ends the CTA's work.
-  auto bar_unit_full = [&](int s) { return bars + 8u * (13 + 2 * C::kStages + s); };
-  auto bar_unit_empty = [&](int s) { return bars + 8u * (15 + 2 * C::kStages + s); };
+  auto bar_unit_full = [&](int s) { return bars + 8u * (11 + 2 * C::kStages + s); };
+  auto bar_unit_empty = [&](int s) { return bars + 8u * (13 + 2 * C::kStages + s); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + C::kMiscOff + 4);
   volatile int* unit_slot = reinterpret_cast<volatile int*>(gbase + C::kMiscOff + 8);
-  constexpr bool kPingPong = (D == 64) ? (FA_ATTN_PINGPONG_D64 != 0) : (FA_ATTN_PINGPONG_D128 != 0);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -348,8 +337,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_o_full(t), 1);
     }
     mbar_init(bar_drain, 1);
-    mbar_init(bar_turn(0), kBM);
-    mbar_init(bar_turn(1), kBM);
     mbar_init(bar_q_empty, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar_unit_full(s), 1);
@@ -586,9 +573,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY;   // reference row max, already scaled (log2 domain)
     float l = 0.f;             // running row sum of exp2(s * sl2 - m_ref)
     const int q_tile0 = q0 + t * kBM;
-    // The turn phases below count the blocks of one unit, so ping-pong builds
-    // launch one unit per CTA (the host never passes a unit counter to them).
-    const bool pingpong = kPingPong && nt[0] > 0 && nt[1] > 0;
     for (int j = 0; j < nt[t]; ++j) {
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 0);
       if (!wwait(bar_s_full(t), (sb + j) & 1)) {
@@ -647,15 +631,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = m_use;
       }
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 2);
-      // Exp phases alternate between the two warpgroups (tile 0 first) so
-      // each has the SM's MUFU throughput to itself while the tensor core
-      // works on the other tile.  Tile 0's turn j follows tile 1's turn j-1;
-      // tile 1's turn j follows tile 0's turn j.
-      if (pingpong && (t == 1 || j > 0) &&
-          !wwait(bar_turn(t), t == 0 ? ((j - 1) & 1) : (j & 1))) {
-        ok = false;
-        break;
-      }
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 3);
       const float neg_m = -m_ref;
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
@@ -701,7 +676,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(bar_p_half(t));
         }
       }
-      if (pingpong) mbar_arrive(bar_turn(1 - t));
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 4);
       if (FA_ATTN_F2 & 2) {
         float a0, a1, b0, b1;
@@ -717,14 +691,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(bar_p_full(t));
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 5);
-    }
-    // Causal units give tile 0 one block fewer than tile 1: pass the turn for
-    // tile 1's last block without work.
-    if (ok && pingpong && t == 0 && nt[0] < nt[1]) {
-      if (wwait(bar_turn(0), (nt[0] - 1) & 1))
-        mbar_arrive(bar_turn(1));
-      else
-        ok = false;
     }
     if (ok && nt[t] > 0 && wwait(bar_o_full(t), ou & 1)) {
       tc_fence_after();
@@ -1405,7 +1371,7 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
   prm.total_units = grid;
   prm.unit_ctr = nullptr;
   prm.tiles_per_unit = tpu;
-  if (FA_ATTN_PERSIST && (q4 || FA_ATTN_PINGPONG_D128 == 0) && grid > sms) {
+  if (FA_ATTN_PERSIST && grid > sms) {
     prm.unit_ctr = ctr;
     grid = sms;
   }
