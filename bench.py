@@ -36,9 +36,8 @@ import torch.distributed as dist  # noqa: E402
 
 from cs348k_fast_attention_grammar_b200.inputs import (ATTN_CONFIGS, MLP_CONFIGS,  # noqa: E402
                                                        make_mlp, make_qkv, pair_tensor)
-from cs348k_fast_attention_grammar_b200.parallel import (gather_shards,  # noqa: E402
-                                                         reduce_error_stats, shard_range,
-                                                         verify_pairs)
+from cs348k_fast_attention_grammar_b200.parallel import (reduce_error_stats,  # noqa: E402
+                                                         shard_range, verify_pairs)
 
 METRIC = "attn fwd TFLOP/s per GPU, % of bf16 tensor peak; box TFLOP/s at 1/2/4/8 GPU"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
@@ -52,8 +51,20 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", choices=sorted(list(ATTN_CONFIGS) + list(MLP_CONFIGS)
-                                               + ["ref512"]),
+                                               + ["ref512", "ln"]),
                     default="cfg2")
+    ap.add_argument("--pairs", type=int, default=0,
+                    help="attention: only the first N (batch, head) pairs (a small case "
+                         "of the same kernel, e.g. for a profiler)")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="cfg3 / ln: only the first N rows of X (a small case)")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="warm-up and timed launches only: no verification, e2e, CPU "
+                         "baseline, comparators or secondary lines (profiler runs)")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the cfg1 / cfg3 lines of the default single-GPU run")
+    ap.add_argument("--no-sdpa", action="store_true",
+                    help="skip the same-GPU torch SDPA (cuDNN) comparator")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="(batch, head) chunks pipelined over the copy/kernel streams")
@@ -178,6 +189,37 @@ def timed_loop(fn, steps: int, world: int, device) -> float:
         ms = t.item()
         dist.barrier()
     return ms
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def timed_reps(fn, reps: int, world: int, device) -> dict:
+    """The reference search's convention (grammar/optimization.py:284-300):
+    ``reps`` calls, each timed alone with CUDA events and synchronised; the
+    minimum is the least noise-contaminated sample.  Max over ranks of each
+    rank's min and median."""
+    stream = torch.cuda.current_stream(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    times = []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for _ in range(reps):
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return {"min_ms": max_over_ranks(min(times), world, device),
+            "median_ms": max_over_ranks(statistics.median(times), world, device),
+            "reps": reps}
 
 
 @contextlib.contextmanager
@@ -310,11 +352,13 @@ def run_reference_mlp(args):
     return 0
 
 
-def workload_config(args, cfg):
+def workload_config(args, cfg, num_pairs=None):
     S, D = cfg["S"], cfg["D"]
-    qkv_bytes = 3 * cfg["B"] * cfg["H"] * S * D * 2
+    n = cfg["B"] * cfg["H"] if num_pairs is None else num_pairs
+    qkv_bytes = 3 * n * S * D * 2
+    sub = "" if n == cfg["B"] * cfg["H"] else f" (first {n} (batch, head) pairs)"
     return {"workload": (f"{args.config}: attention forward {'causal' if cfg['causal'] else 'non-causal'}"
-                         f" bf16 B={cfg['B']} H={cfg['H']} S={S} D={D}"),
+                         f" bf16 B={cfg['B']} H={cfg['H']} S={S} D={D}{sub}"),
             "B": cfg["B"], "H": cfg["H"], "S": S, "D": D, "causal": cfg["causal"],
             "seed": cfg["seed"], "parallelism": f"dp over batch*head x {args.gpus}",
             "l2": (f"inputs larger than L2 ({qkv_bytes / 2**20:.0f} MiB of Q/K/V per step "
@@ -346,6 +390,8 @@ def main(argv=None):
         line = bench_mlp(args, fab, device, world, rank)
     elif args.config == "ref512":
         line = bench_ref512(args, fab, device, world, rank)
+    elif args.config == "ln":
+        line = bench_ln(args, fab, device, world, rank)
     else:
         line = bench_attention(args, fab, device, world, rank)
     if rank == 0:
@@ -368,23 +414,75 @@ def roofline(achieved_tflops, peaks, traffic):
     return out
 
 
-def bench_attention(args, fab, device, world, rank):
-    cfg = ATTN_CONFIGS[args.config]
-    num_pairs = cfg["B"] * cfg["H"]
-    pairs = shard_range(num_pairs, world, rank)
+def attention_timing(args, fab, cfg, pairs, device, world, steps, warmup):
+    """Seeded Q/K/V for ``pairs`` on this GPU, ``warmup`` untimed launches,
+    then ``steps`` timed ones (window mean, clocks sampled meanwhile) and five
+    individually timed reps (min / median)."""
     q, k, v = make_qkv(cfg, pairs, device)
     o = torch.empty_like(q)
     step = lambda: fab.attention(q, k, v, causal=cfg["causal"], out=o)  # noqa: E731
-    for _ in range(max(args.warmup, 0)):
+    for _ in range(max(warmup, 0)):
         step()
     torch.cuda.synchronize()
     with ClockSampler(local_index(device)) as clk:
-        ms = timed_loop(step, args.steps, world, device)
-    flops_total = attn_flops(cfg)
+        ms = timed_loop(step, steps, world, device)
+    reps = timed_reps(step, 5, world, device)
+    return {"q": q, "k": k, "v": v, "o": o, "ms": ms, "reps": reps, "clocks": clk.summary()}
+
+
+def sdpa_same_gpu(q, k, v, o, causal, flops_local, steps, warmup, world, device):
+    """torch scaled_dot_product_attention with the cuDNN backend on the same
+    tensors, timed the same way (a library comparator, not this repo's path),
+    plus the largest difference between its output and ours."""
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            f = lambda: torch.nn.functional.scaled_dot_product_attention(  # noqa: E731
+                q, k, v, is_causal=causal)
+            for _ in range(max(warmup, 1)):
+                ref = f()
+            torch.cuda.synchronize()
+            ms = timed_loop(f, steps, world, device)
+        n = min(4, q.shape[1])
+        diff = (ref[:, :n].float() - o[:, :n].float()).abs().max().item()
+        del ref
+        tf = flops_local / (ms * 1e-3) / 1e12
+        return {"value": tf, "unit": "TFLOP/s per GPU", "ms_per_step": ms,
+                "max_abs_diff_vs_ours": diff,
+                "what": "torch SDPA, cuDNN backend, same bf16 tensors, same event window"}
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+
+
+def bench_attention(args, fab, device, world, rank):
+    cfg = ATTN_CONFIGS[args.config]
+    num_pairs = cfg["B"] * cfg["H"] if args.pairs <= 0 else min(args.pairs, cfg["B"] * cfg["H"])
+    pairs = shard_range(num_pairs, world, rank)
+    t = attention_timing(args, fab, cfg, pairs, device, world, args.steps, args.warmup)
+    q, k, v, o, ms = t["q"], t["k"], t["v"], t["o"], t["ms"]
+    flops_total = attn_flops(cfg, num_pairs)
     value = flops_total / (ms * 1e-3) / 1e12
     flops_local = attn_flops(cfg, len(pairs))
     achieved = flops_local / (ms * 1e-3) / 1e12
     peaks = load_peaks()
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "ms_per_step_min": t["reps"]["min_ms"], "reps": t["reps"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": f"synthetic: seeded N(0,1)*{cfg['amp']} per (batch, head) pair (Philox), bf16",
+        "config": workload_config(args, cfg, num_pairs),
+        "per_gpu_tflops": value / world,
+        "pct_of_peak": 100.0 * achieved / peaks["bf16_tflops"],
+        "roofline": roofline(achieved, peaks,
+                             load_traffic(args.config) if args.pairs <= 0 else None),
+        "gpu_launches": args.steps,
+        "clocks": t["clocks"],
+        "flops_per_step": flops_total,
+        "flop_convention": "4*B*H*S^2*D, halved when causal (old/benchmark.py:131)",
+    }
+    if args.kernel_only:
+        return line
 
     # verification: seeded subset of pairs vs a torch fp32 reference, per owner
     vp = verify_pairs(num_pairs, args.verify_pairs)
@@ -400,46 +498,102 @@ def bench_attention(args, fab, device, world, rank):
     verify = reduce_error_stats(max_abs, sum_abs, count, device)
     verify.update({"pairs": len(vp), "ok": verify["max_abs"] <= 2e-2 and verify["mean_abs"] <= 2e-3,
                    "reference": "torch fp32 on GPU, per pair"})
+    line["verify"] = verify
 
-    gather_ms = None
+    if not args.no_sdpa:
+        line["sdpa_same_gpu"] = sdpa_same_gpu(q, k, v, o, cfg["causal"], flops_local,
+                                              args.steps, args.warmup, world, device)
     if world > 1:
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        full = gather_shards(o, world, rank, num_pairs)
-        torch.cuda.synchronize()
-        gather_ms = 1e3 * (time.perf_counter() - t0)
-        del full
+        line["gather"] = timed_gather(o, world, rank, device)
+        line["gather_ms"] = line["gather"]["ms"]
 
-    e2e = None
     if not args.no_e2e:
-        e2e = attention_e2e(args, fab, cfg, q, k, v, world, device, flops_total)
+        line["e2e"] = attention_e2e(args, fab, cfg, q, k, v, world, device, flops_total)
+        line["host_link"] = host_link_probe(world, device)
 
-    cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, npairs_cpu, secs = cpu_attention_sample(cfg, args.cpu_seconds)
-        cpu = {"value": tf, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"{npairs_cpu} (batch, head) pairs of {args.config} in {secs:.1f} s "
-                         "(pairs are independent; throughput scales linearly)",
-               "cpu": cpu_model(),
-               "what": "oracle.naive_torch_pair: correct restatement of pytorch-naive.py:41-63"}
-    return {
-        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": f"synthetic: seeded N(0,1)*{cfg['amp']} per (batch, head) pair (Philox), bf16",
-        "config": workload_config(args, cfg),
-        "per_gpu_tflops": value / world,
-        "pct_of_peak": 100.0 * achieved / peaks["bf16_tflops"],
-        "roofline": roofline(achieved, peaks, load_traffic(args.config)),
-        "cpu_baseline": cpu,
-        "e2e": e2e,
-        "gpu_launches": args.steps,
-        "clocks": clk.summary(),
-        "verify": verify,
-        "gather_ms": gather_ms,
-        "flops_per_step": flops_total,
-        "flop_convention": "4*B*H*S^2*D, halved when causal (old/benchmark.py:131)",
-    }
+        line["cpu_baseline"] = {
+            "value": tf, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{npairs_cpu} (batch, head) pairs of {args.config} in {secs:.1f} s "
+                      "(pairs are independent; throughput scales linearly)",
+            "cpu": cpu_model(),
+            "what": "oracle.naive_torch_pair: correct restatement of pytorch-naive.py:41-63"}
+    else:
+        line["cpu_baseline"] = None
+
+    del q, k, v, o, t
+    if world == 1 and args.config == "cfg2" and args.pairs <= 0 and not args.no_secondary:
+        line["secondary"] = secondary_lines(args, fab, device, peaks)
+    return line
+
+
+def secondary_lines(args, fab, device, peaks):
+    """The other single-GPU BASELINE configurations, device-timed on the same
+    box as the headline: cfg1 (D = 64, non-causal) with its cuDNN comparator,
+    and the cfg3 MLP block."""
+    out = {}
+    cfg = ATTN_CONFIGS["cfg1"]
+    n = cfg["B"] * cfg["H"]
+    t = attention_timing(args, fab, cfg, range(n), device, 1, args.steps, args.warmup)
+    flops = attn_flops(cfg, n)
+    tf = flops / (t["ms"] * 1e-3) / 1e12
+    ref = torch_ref_pair(t["q"][0, 0], t["k"][0, 0], t["v"][0, 0], cfg["causal"])
+    err = (t["o"][0, 0].float() - ref).abs()
+    out["cfg1"] = {"workload": "attention forward non-causal bf16 B=8 H=16 S=4096 D=64",
+                   "value": tf, "unit": "TFLOP/s", "ms_per_step": t["ms"],
+                   "ms_per_step_min": t["reps"]["min_ms"],
+                   "roofline": roofline(tf, peaks, load_traffic("cfg1")),
+                   "clocks": t["clocks"], "gpu_launches": args.steps,
+                   "verify": {"pairs": 1, "max_abs": err.max().item(),
+                              "mean_abs": err.mean().item()}}
+    if not args.no_sdpa:
+        out["cfg1"]["sdpa_same_gpu"] = sdpa_same_gpu(t["q"], t["k"], t["v"], t["o"],
+                                                     cfg["causal"], flops, args.steps,
+                                                     args.warmup, 1, device)
+    del t, ref, err
+    m = mlp_timing(args, fab, MLP_CONFIGS["cfg3"], MLP_CONFIGS["cfg3"]["M"], device, 1)
+    out["cfg3"] = {"workload": "MLP block Y = gelu_tanh(X W1) W2, M=8192 K=4096 N=16384 bf16",
+                   "value": m["value"], "unit": "TFLOP/s", "ms_per_step": m["ms"],
+                   "ms_per_step_min": m["reps"]["min_ms"],
+                   "roofline": roofline(m["dominant_tflops"], peaks, load_traffic("cfg3")),
+                   "gemm_ms": m["gemm_ms"], "clocks": m["clocks"],
+                   "gpu_launches": 2 * args.steps, "verify": m["verify"]}
+    return out
+
+
+def timed_gather(o, world, rank, device, reps=3):
+    """NCCL gather of the O shards on rank 0: one untimed gather (communicator
+    and channel set-up), then ``reps`` gathers timed with CUDA events, max over
+    ranks.  GB/s counts the bytes that land on rank 0 from the other ranks."""
+    bufs = [torch.empty_like(o) for _ in range(world)] if rank == 0 else None
+
+    def once():
+        dist.gather(o, gather_list=bufs, dst=0)
+    once()
+    torch.cuda.synchronize()
+    ms = timed_loop(once, reps, world, device)
+    moved = (world - 1) * o.numel() * o.element_size()
+    return {"ms": ms, "gbs_into_rank0": moved / (ms * 1e-3) / 1e9, "bytes_into_rank0": moved,
+            "reps": reps, "what": "warm dist.gather of the O shards (NCCL), CUDA events"}
+
+
+def host_link_probe(world, device, nbytes=512 << 20, reps=3):
+    """Plain pinned-host <-> device copies (one cudaMemcpyAsync each), every
+    rank at once, timed with CUDA events: the host-link bound that the e2e
+    figure runs against.  Max over ranks; the aggregate is world x bytes over
+    that time."""
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    out = {"bytes_per_gpu": nbytes, "reps": reps}
+    for name, fn in (("h2d", lambda: d.copy_(h, non_blocking=True)),
+                     ("d2h", lambda: h.copy_(d, non_blocking=True))):
+        fn()
+        torch.cuda.synchronize()
+        ms = timed_loop(fn, reps, world, device)
+        out[f"{name}_gbs_per_gpu"] = nbytes / (ms * 1e-3) / 1e9
+        out[f"{name}_gbs_aggregate"] = world * nbytes / (ms * 1e-3) / 1e9
+    return out
 
 
 def local_index(device) -> int:
@@ -559,16 +713,14 @@ def run_reference_ref512(args):
     return 0
 
 
-def bench_mlp(args, fab, device, world, rank):
-    """MLP block, rows of X sharded over the ranks (weights replicated; every
-    rank regenerates the same seeded tensors and keeps its row block), Y
-    gathered on rank 0 after timing and spot-checked against a torch fp32
-    reference."""
-    import oracle
-    cfg = MLP_CONFIGS[args.config]
-    x_full, w1, w2 = make_mlp(cfg, device)
-    M, K, N = cfg["M"], cfg["K"], cfg["N"]
-    rows = shard_range(M, world, rank)
+def mlp_timing(args, fab, cfg, rows_total, device, world, rank=0):
+    """This rank's row block of the first ``rows_total`` rows of X with the
+    full weights: warm-up, timed MLP blocks (window mean, clocks), five
+    individually timed reps, per-GEMM durations, and a 32-row spot check
+    against a torch fp32 reference."""
+    x_full, w1, w2 = make_mlp(dict(cfg, M=rows_total), device)
+    K, N = cfg["K"], cfg["N"]
+    rows = shard_range(rows_total, world, rank)
     x = x_full[rows.start:rows.stop].contiguous()
     del x_full
     Mr = x.shape[0]
@@ -577,8 +729,10 @@ def bench_mlp(args, fab, device, world, rank):
     step = lambda: fab.mlp(x, w1, w2, act="gelu_tanh", hidden=hidden, out=y)  # noqa: E731
     for _ in range(max(args.warmup, 0)):
         step()
+    torch.cuda.synchronize()
     with ClockSampler(local_index(device)) as clk:
         ms = timed_loop(step, args.steps, world, device)
+    reps = timed_reps(step, 5, world, device)
     # per-GEMM durations for the roofline of the dominant kernel
     stream = torch.cuda.current_stream(device)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
@@ -592,12 +746,8 @@ def bench_mlp(args, fab, device, world, rank):
         torch.cuda.synchronize()
         g1.append(ev[0].elapsed_time(ev[1]))
         g2.append(ev[1].elapsed_time(ev[2]))
-    gemm_flops = 2.0 * Mr * K * N
     t1, t2 = statistics.mean(g1), statistics.mean(g2)
-    dom = max(t1, t2)
-    flops = float(oracle.mlp_flops(M, K, N))
-    value = flops / (ms * 1e-3) / 1e12
-    # spot check: 32 seeded rows of this rank's block vs torch fp32 (hidden in bf16)
+    gemm_flops = 2.0 * Mr * K * N
     sel = torch.from_numpy(__import__("numpy").random.default_rng(rank).choice(
         Mr, min(32, Mr), replace=False)).to(device)
     h = torch.nn.functional.gelu(x[sel].float() @ w1.float(), approximate="tanh")
@@ -606,6 +756,41 @@ def bench_mlp(args, fab, device, world, rank):
     verify = reduce_error_stats(d.max().item(), d.sum().item(), d.numel(), device)
     verify.update({"ok": verify["max_abs"] <= 2e-2 and verify["mean_abs"] <= 2e-3,
                    "reference": "torch fp32 on GPU, 32 rows per rank"})
+    flops = 4.0 * rows_total * K * N
+    return {"x": x, "w1": w1, "w2": w2, "y": y, "ms": ms, "reps": reps,
+            "clocks": clk.summary(), "value": flops / (ms * 1e-3) / 1e12, "flops": flops,
+            "gemm_ms": {"gemm1_gelu": t1, "gemm2": t2},
+            "dominant_tflops": gemm_flops / (max(t1, t2) * 1e-3) / 1e12, "verify": verify}
+
+
+def bench_mlp(args, fab, device, world, rank):
+    """MLP block, rows of X sharded over the ranks (weights replicated; every
+    rank regenerates the same seeded tensors and keeps its row block), Y
+    gathered on rank 0 after timing (warm, event-timed) and spot-checked
+    against a torch fp32 reference."""
+    import oracle
+    cfg = MLP_CONFIGS[args.config]
+    K, N = cfg["K"], cfg["N"]
+    M = cfg["M"] if args.rows <= 0 else min(args.rows, cfg["M"])
+    m = mlp_timing(args, fab, cfg, M, device, world, rank)
+    x, w1, w2, y, ms = m["x"], m["w1"], m["w2"], m["y"], m["ms"]
+    Mr = x.shape[0]
+    peaks = load_peaks()
+    line = {"metric": "MLP block TFLOP/s", "value": m["value"], "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "ms_per_step_min": m["reps"]["min_ms"], "reps": m["reps"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic: X~N(0,1), W~N(0,1/fan_in), bf16",
+            "config": {"workload": f"{args.config}: Y=gelu_tanh(X W1) W2, M={M} K={K} N={N}",
+                       "parallelism": f"rows of X over {world} ranks, weights replicated",
+                       "l2": "inputs larger than L2 (X 64 MiB + W1 128 MiB + W2 128 MiB)"},
+            "pct_of_peak": 100.0 * m["value"] / world / peaks["bf16_tflops"],
+            "roofline": roofline(m["dominant_tflops"], peaks,
+                                 load_traffic(args.config) if args.rows <= 0 else None),
+            "gemm_ms": m["gemm_ms"], "gpu_launches": 2 * args.steps, "clocks": m["clocks"],
+            "verify": m["verify"]}
+    if args.kernel_only:
+        return line
     e2e = None
     if not args.no_e2e:
         # Same metric through the public API with X streamed from pinned host
@@ -619,10 +804,12 @@ def bench_mlp(args, fab, device, world, rank):
         torch.cuda.synchronize()
         steps = max(1, args.e2e_steps)
         ms_e2e = timed_loop(e2e_step, steps, world, device)
-        e2e = {"value": flops / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_e2e,
-               "steps": steps, "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * K * 2,
+        e2e = {"value": m["flops"] / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "ms_per_step": ms_e2e, "steps": steps, "h2d_bytes_per_step": M * K * 2,
+               "d2h_bytes_per_step": M * K * 2,
                "path": "mlp_from_host: pinned host X -> device -> host Y, rows in 4 chunks "
                        "pipelined over copy-in / GEMMs / copy-out streams; weights resident"}
+    line["e2e"] = e2e
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(host_cores())
@@ -640,32 +827,38 @@ def bench_mlp(args, fab, device, world, rank):
                          "rows are independent",
                "cpu": cpu_model(),
                "what": "fp32 torch gelu_tanh(X W1) W2, the oracle's MLP formula"}
-    gather_ms = None
+    line["cpu_baseline"] = cpu
     if world > 1 and M % world == 0:
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        if rank == 0:
-            bufs = [torch.empty_like(y) for _ in range(world)]
-            dist.gather(y, gather_list=bufs, dst=0)
-            del bufs
-        else:
-            dist.gather(y, dst=0)
-        torch.cuda.synchronize()
-        gather_ms = 1e3 * (time.perf_counter() - t0)
+        line["gather"] = timed_gather(y.view(1, Mr, K), world, rank, device)
+        line["gather_ms"] = line["gather"]["ms"]
+    return line
+
+
+def bench_ln(args, fab, device, world, rank):
+    """Row LayerNorm alone (the last stage of the reference's MLP block) on
+    ``--rows`` rows of cfg3's feature width: an HBM-bound kernel."""
+    K = MLP_CONFIGS["cfg3"]["K"]
+    rows = args.rows if args.rows > 0 else 16384
+    g = torch.Generator(device=device).manual_seed(0)
+    x = torch.randn((rows, K), generator=g, device=device).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    step = lambda: fab.layer_norm_rows(x, out=y)  # noqa: E731
+    for _ in range(max(args.warmup, 0)):
+        step()
+    torch.cuda.synchronize()
+    with ClockSampler(local_index(device)) as clk:
+        ms = timed_loop(step, args.steps, world, device)
+    nbytes = 4.0 * rows * K
+    gbs = nbytes / (ms * 1e-3) / 1e9
     peaks = load_peaks()
-    return {"metric": "MLP block TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic: X~N(0,1), W~N(0,1/fan_in), bf16",
-            "config": {"workload": f"{args.config}: Y=gelu_tanh(X W1) W2, M={M} K={K} N={N}",
-                       "parallelism": f"rows of X over {world} ranks, weights replicated",
-                       "l2": "inputs larger than L2 (X 64 MiB + W1 128 MiB + W2 128 MiB)"},
-            "pct_of_peak": 100.0 * value / world / peaks["bf16_tflops"],
-            "roofline": roofline(gemm_flops / (dom * 1e-3) / 1e12, peaks,
-                                 load_traffic(args.config)),
-            "gemm_ms": {"gemm1_gelu": t1, "gemm2": t2},
-            "gpu_launches": 2 * args.steps, "clocks": clk.summary(), "cpu_baseline": cpu,
-            "e2e": e2e, "verify": verify, "gather_ms": gather_ms}
+    return {"metric": "row LayerNorm GB/s", "value": gbs * world, "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: N(0,1) bf16",
+            "config": {"workload": f"ln: row LayerNorm {rows} x {K} bf16 (no affine)"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"], "traffic": None},
+            "gpu_launches": args.steps, "clocks": clk.summary()}
 
 
 if __name__ == "__main__":

@@ -34,8 +34,10 @@ SIGNATURES = {
     "fa_mlp_ln_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
                                _c_float, _vp]),
     "fa_layernorm_rows": (_c_int, [_vp, _vp, _c_int, _c_int, _i64, _i64, _c_float, _vp]),
+    "fa_mlp_fwd_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp]),
     "fa_device_status": (_c_int, []),
     "fa_selftest_wait_timeout": (_c_int, [_c_int, _vp]),
+    "fa_selftest_exp2": (_c_int, [_vp, _vp, _c_int, _vp]),
 }
 
 _lock = threading.Lock()

@@ -22,7 +22,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_NAME = "libfa_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 SOURCES = ["common.cu", "attn_fwd.cu", "gemm.cu"]
-HEADERS = ["sm100_ptx.cuh", "sm100_tmem_wide.cuh", "fa_internal.h"]
+HEADERS = ["sm100_ptx.cuh", "sm100_tmem_wide.cuh", "sm100_2sm.cuh", "fa_internal.h"]
 PUBLIC_HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "fa_b200.h")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -782,15 +782,10 @@ int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
                 const AttnParams& prm, int grid, cudaStream_t stream, bool pdl) {
   using C = AttnCfg<D>;
   auto kern = attn_fwd_kernel<D, CAUSAL, OUT_F32>;
-  static bool attr_set[64] = {};
+  static KernelPrep prep;
   int dev = 0;
-  int rc = FA_OK;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FA_ERR_CUDA;
-  if (!attr_set[dev]) {
-    rc = prepare_device(reinterpret_cast<const void*>(kern), C::kSmemBytes, &dev);
-    if (rc != FA_OK) return rc;
-    attr_set[dev] = true;
-  }
+  const int rc = prepare_kernel(prep, reinterpret_cast<const void*>(kern), C::kSmemBytes, &dev);
+  if (rc != FA_OK) return rc;
   return launch_maybe_pdl(kern, grid, kThreads, C::kSmemBytes, stream, pdl, mq, mk, mv, prm);
 }
 
@@ -1253,15 +1248,10 @@ int launch_attn_q4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
                    const AttnParams& prm, int grid, cudaStream_t stream, bool pdl) {
   using C = AttnQ4Cfg;
   auto kern = attn_fwd_q4_kernel<CAUSAL, OUT_F32>;
-  static bool attr_set[64] = {};
+  static KernelPrep prep;
   int dev = 0;
-  int rc = FA_OK;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FA_ERR_CUDA;
-  if (!attr_set[dev]) {
-    rc = prepare_device(reinterpret_cast<const void*>(kern), C::kSmemBytes, &dev);
-    if (rc != FA_OK) return rc;
-    attr_set[dev] = true;
-  }
+  const int rc = prepare_kernel(prep, reinterpret_cast<const void*>(kern), C::kSmemBytes, &dev);
+  if (rc != FA_OK) return rc;
   return launch_maybe_pdl(kern, grid, kQ4Threads, C::kSmemBytes, stream, pdl, mq, mk, mv, prm);
 }
 
@@ -1432,8 +1422,42 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Self test of the softmax's exponentials on the device: for each x,
+// out[i] = exp2_fma(x), out[n + i] = exp2_fma_x2 on the pair containing x,
+// out[2n + i] = ex2.approx(x) -- the routines the attention kernels call.
+__global__ void __launch_bounds__(256)
+    exp2_selftest_kernel(const float* __restrict__ x, float* __restrict__ out, int n) {
+  const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const float x0 = x[i];
+  const float x1 = (i + 1 < n) ? x[i + 1] : 0.f;
+  float a0, a1;
+  exp2_fma_x2(x0, x1, a0, a1);
+  out[i] = exp2_fma(x0);
+  out[n + i] = a0;
+  out[2 * n + i] = ex2_approx(x0);
+  if (i + 1 < n) {
+    out[i + 1] = exp2_fma(x1);
+    out[n + i + 1] = a1;
+    out[2 * n + i + 1] = ex2_approx(x1);
+  }
+}
+
 }  // namespace
 }  // namespace fa
+
+extern "C" int fa_selftest_exp2(const float* x, float* out, int n, void* stream) {
+  using namespace fa;
+  if (!x || !out) return FA_ERR_NULL;
+  if (n <= 0 || n > (1 << 28)) return FA_ERR_SHAPE;
+  int dev = 0;
+  const int rc = prepare_device(nullptr, 0, &dev);
+  if (rc != FA_OK) return rc;
+  const int threads = 256;
+  const int blocks = ((n + 1) / 2 + threads - 1) / threads;
+  exp2_selftest_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(x, out, n);
+  return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
+}
 
 extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int H,
                            int S, int D, const int64_t* st, int causal, float scale,

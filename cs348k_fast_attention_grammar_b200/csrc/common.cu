@@ -55,6 +55,34 @@ int prepare_device(const void* kernel_fn, int smem_bytes, int* device_out) {
   return FA_OK;
 }
 
+int prepare_kernel(KernelPrep& prep, const void* kernel_fn, int smem_bytes, int* device_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return FA_ERR_DEVICE;
+  *device_out = dev;
+  if (prep.done[dev].load(std::memory_order_acquire)) return FA_OK;
+  static std::mutex prep_mu;
+  std::lock_guard<std::mutex> lk(prep_mu);
+  if (prep.done[dev].load(std::memory_order_relaxed)) return FA_OK;
+  const int rc = prepare_device(kernel_fn, smem_bytes, &dev);
+  if (rc != FA_OK) return rc;
+  prep.done[dev].store(true, std::memory_order_release);
+  return FA_OK;
+}
+
+int sm_count(int dev) {
+  static std::atomic<int> n_sms[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return 0;
+  int n = n_sms[dev].load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  n_sms[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
 int* device_status_ptr() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;

@@ -2,6 +2,7 @@
 // public C ABI, which is include/fa_b200.h).
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -21,6 +22,18 @@ EncodeTiledFn encode_tiled_fn();
 // Checks that the current device is an sm_100 part and that the kernel's
 // dynamic shared memory attribute has been raised on it (once per device).
 int prepare_device(const void* kernel_fn, int smem_bytes, int* device_out);
+
+// One kernel's per-device set-up state.  prepare_kernel() runs the set-up
+// (sm_100 check, dynamic shared-memory limit) under a library mutex the first
+// time the kernel is used on a device and publishes it through an atomic
+// flag, so later calls -- from any thread -- only read the flag.
+struct KernelPrep {
+  std::atomic<bool> done[64] = {};
+};
+int prepare_kernel(KernelPrep& prep, const void* kernel_fn, int smem_bytes, int* device_out);
+
+// Number of SMs of device dev (cached; 0 if the query failed).
+int sm_count(int dev);
 
 // Device-global status word written by kernels (fa::kDevTimeout ...).
 int* device_status_ptr();

@@ -16,6 +16,7 @@
 //               epilogue of tile i overlap the main loop of tile i+1.
 #include <cuda_bf16.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "fa_internal.h"
@@ -449,21 +450,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
   }
 }
 
-int g_num_sms[64] = {};
-bool g_gemm_attr[64] = {};
-int g_clusters_2sm[64] = {};     // co-resident clusters of gemm_act_2sm_kernel
+KernelPrep g_gemm_prep;
+std::mutex g_clusters_mu;
+std::atomic<int> g_clusters_2sm[64] = {};   // co-resident clusters of gemm_act_2sm_kernel
+
+// Set-up of the two-SM kernel on device dev (once): shared-memory limit and
+// the number of clusters that fit on the device at once.
+int clusters_2sm(int dev, int* n_out) {
+  int n = g_clusters_2sm[dev].load(std::memory_order_acquire);
+  if (n > 0) {
+    *n_out = n;
+    return FA_OK;
+  }
+  std::lock_guard<std::mutex> lk(g_clusters_mu);
+  n = g_clusters_2sm[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaFuncSetAttribute(gemm_act_2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kG2SmemBytes) != cudaSuccess)
+      return FA_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74);
+    cfg.blockDim = dim3(kGThreads);
+    cfg.dynamicSmemBytes = kG2SmemBytes;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_act_2sm_kernel, &cfg) != cudaSuccess || n <= 0)
+      n = (sm_count(dev) > 0 ? sm_count(dev) : 148) / 2;
+    (void)cudaGetLastError();
+    g_clusters_2sm[dev].store(n, std::memory_order_release);
+  }
+  *n_out = n;
+  return FA_OK;
+}
 
 int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int64_t lda,
                 int64_t ldb, int64_t ldc, int act, cudaStream_t stream,
                 const void* res = nullptr, int64_t ldr = 0) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FA_ERR_CUDA;
-  if (!g_gemm_attr[dev]) {
-    int rc = prepare_device(reinterpret_cast<const void*>(gemm_act_kernel), kGSmemBytes, &dev);
+  {
+    const int rc = prepare_kernel(g_gemm_prep, reinterpret_cast<const void*>(gemm_act_kernel),
+                                  kGSmemBytes, &dev);
     if (rc != FA_OK) return rc;
-    cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    g_gemm_attr[dev] = true;
   }
+  const int num_sms = sm_count(dev);
   CUtensorMap ma, mb;
   int rc = make_tmap_2d(&ma, a, M, K, lda, kGBM, 64);
   if (rc != FA_OK) return rc;
@@ -498,25 +525,13 @@ int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int6
   p.status = device_status_ptr();
   if (p.status == nullptr) return FA_ERR_CUDA;
   if (two_sm) {
-    if (g_clusters_2sm[dev] == 0) {
-      if (cudaFuncSetAttribute(gemm_act_2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kG2SmemBytes) != cudaSuccess)
-        return FA_ERR_CUDA;
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(2 * 74);
-      cfg.blockDim = dim3(kGThreads);
-      cfg.dynamicSmemBytes = kG2SmemBytes;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, gemm_act_2sm_kernel, &cfg) != cudaSuccess || n <= 0)
-        n = (g_num_sms[dev] > 0 ? g_num_sms[dev] : 148) / 2;
-      cudaGetLastError();
-      g_clusters_2sm[dev] = n;
-    }
-    const int grid = 2 * min(p.num_tiles, g_clusters_2sm[dev]);
+    int clusters = 0;
+    if ((rc = clusters_2sm(dev, &clusters)) != FA_OK) return rc;
+    const int grid = 2 * min(p.num_tiles, clusters);
     gemm_act_2sm_kernel<<<grid, kGThreads, kG2SmemBytes, stream>>>(ma, mb, p);
     return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
   }
-  const int grid = min(p.num_tiles, g_num_sms[dev] > 0 ? g_num_sms[dev] : 148);
+  const int grid = min(p.num_tiles, num_sms > 0 ? num_sms : 148);
   gemm_act_kernel<<<grid, kGThreads, kGSmemBytes, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
@@ -556,16 +571,18 @@ static __device__ __align__(256) __nv_bfloat16 g_mlp_hidden_scratch[kNoAllocHidd
 std::mutex g_scratch_mu;
 void* g_scratch_addr[64] = {};
 
-// Device address of g_mlp_hidden_scratch on the current device, looked up
-// once per device (the first call on a device does the lookup).
-int hidden_scratch_address(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FA_ERR_CUDA;
+// Device address of g_mlp_hidden_scratch on device dev (already checked to be
+// an sm_100 part), looked up once per device: the first call on a device does
+// the lookup.  A failed lookup clears the runtime's last-error word so that
+// the failure is not reported again by the next launch check.
+int hidden_scratch_address(int dev, void** out) {
   std::lock_guard<std::mutex> lk(g_scratch_mu);
   if (g_scratch_addr[dev] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_mlp_hidden_scratch) != cudaSuccess || p == nullptr)
+    if (cudaGetSymbolAddress(&p, g_mlp_hidden_scratch) != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();
       return FA_ERR_CUDA;
+    }
     g_scratch_addr[dev] = p;
   }
   *out = g_scratch_addr[dev];
@@ -579,13 +596,18 @@ extern "C" int fa_mlp_fwd_noalloc(const void* x, const void* w1, const void* w2,
                                   int K, int N, int act, void* stream) {
   if (M > 0 && N > 0 && static_cast<int64_t>(M) * N > fa::kNoAllocHiddenElems)
     return FA_ERR_SCRATCH;
+  // Argument checks come before any CUDA call, with a stand-in for the hidden
+  // array (non-null, 256-byte aligned like the array itself), so a bad
+  // argument gets its own status code on any machine.
+  const void* hidden_standin = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  int rc = fa::check_gemm_args(x, w1, hidden_standin, M, N, K, K, N, N, act);
+  if (rc != FA_OK) return rc;
+  rc = fa::check_gemm_args(hidden_standin, w2, y, M, K, N, N, K, K, FA_ACT_NONE);
+  if (rc != FA_OK) return rc;
+  int dev = 0;
+  if ((rc = fa::prepare_device(nullptr, 0, &dev)) != FA_OK) return rc;
   void* hidden = nullptr;
-  int rc = fa::hidden_scratch_address(&hidden);
-  if (rc != FA_OK) return rc;
-  rc = fa::check_gemm_args(x, w1, hidden, M, N, K, K, N, N, act);
-  if (rc != FA_OK) return rc;
-  rc = fa::check_gemm_args(hidden, w2, y, M, K, N, N, K, K, FA_ACT_NONE);
-  if (rc != FA_OK) return rc;
+  if ((rc = fa::hidden_scratch_address(dev, &hidden)) != FA_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   rc = fa::launch_gemm(x, w1, hidden, M, N, K, K, N, N, act, s);
   if (rc != FA_OK) return rc;

@@ -178,6 +178,17 @@ int fa_mlp_fwd_noalloc(const void* x, const void* w1, const void* w2, void* y, i
 int fa_selftest_wait_timeout(int limit_us, void* stream);
 
 /*
+ * Self test of the attention softmax's exponentials on the device: for the
+ * n fp32 values x, writes out[i] = the FMA-pipe 2^x (Cody-Waite style
+ * round-to-nearest range reduction, degree-3 minimax polynomial, exponent
+ * add), out[n + i] = the same computed two at a time with paired fp32
+ * instructions, and out[2n + i] = ex2.approx(x) (MUFU).  out holds 3n
+ * floats.  These are the routines the attention kernels call.  Reference
+ * analog: the exp stage that run_attention_search.py:64-67 lowers to ct.exp.
+ */
+int fa_selftest_exp2(const float* x, float* out, int n, void* stream);
+
+/*
  * Reads and clears the device-side status word of the current device
  * (FA_OK, or FA_ERR_TIMEOUT when a kernel's bounded wait ran out).
  * Synchronises the device.

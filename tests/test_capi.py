@@ -36,9 +36,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 def test_python_binding_covers_header():
     bound = set(_lib.SIGNATURES)
     declared = set(_declared_functions())
-    # every bound name is declared; the no-alloc variant is bound where used
-    assert bound <= declared
-    assert declared - bound <= {"fa_mlp_fwd_noalloc"}
+    assert bound == declared
 
 
 def test_strerror_for_every_status_code():
@@ -84,9 +82,16 @@ def test_argument_checks_without_device():
         codes["FA_ERR_STRIDE"]
     assert lib.fa_selftest_wait_timeout(0, None) == codes["FA_ERR_ARG"]
     fn = lib.fa_mlp_fwd_noalloc
-    fn.restype = ctypes.c_int
-    fn.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
     assert fn(p, p, p, p, 4096, 64, 4096, 2, None) == codes["FA_ERR_SCRATCH"]
+    assert fn(p, p, p, p, 2049, 64, 4096, 2, None) == codes["FA_ERR_SCRATCH"]
+    # argument checks precede every CUDA call, so they hold without a device
+    assert fn(None, p, p, p, 128, 64, 256, 2, None) == codes["FA_ERR_NULL"]
+    assert fn(p, p, p, None, 128, 64, 256, 2, None) == codes["FA_ERR_NULL"]
+    assert fn(p, p, p, p, 128, 64, 100, 2, None) == codes["FA_ERR_SHAPE"]
+    assert fn(p, p, p, p, 128, 60, 256, 2, None) == codes["FA_ERR_SHAPE"]
+    assert fn(p, p, p, p, 0, 64, 256, 2, None) == codes["FA_ERR_SHAPE"]
+    assert fn(p, p, p, p, 128, 64, 256, 9, None) == codes["FA_ERR_ARG"]
+    assert fn(odd, p, p, p, 128, 64, 256, 2, None) == codes["FA_ERR_ALIGN"]
 
 
 def test_no_cpu_fallback_in_package():

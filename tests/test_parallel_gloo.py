@@ -101,3 +101,51 @@ def test_rank_failure_surfaces_as_error(tmp_path):
         mp.start_processes(_worker, args=(2, _free_port(), path, 1), nprocs=2, join=True,
                            start_method="spawn")
     assert not os.path.exists(path)
+
+
+MLP_CFG = dict(M=96, K=64, N=128, seed=13)
+
+
+def _mlp_worker(rank, world, port, result_path):
+    """The MLP line's multi-rank logic (bench.py --config cfg3 under torchrun):
+    rows of X sharded over the ranks with replicated weights, every rank
+    regenerating the same seeded tensors, Y gathered on rank 0 and a seeded
+    spot check of rows reduced over the ranks (the oracle stands in for the
+    GEMM kernels here)."""
+    import oracle
+    from cs348k_fast_attention_grammar_b200.inputs import make_mlp
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=30))
+    try:
+        x_full, w1, w2 = make_mlp(MLP_CFG, "cpu")
+        rows = shard_range(MLP_CFG["M"], world, rank)
+        x = x_full[rows.start:rows.stop]
+        y = torch.from_numpy(oracle.mlp(x.float().numpy(), w1.float().numpy(),
+                                        w2.float().numpy(), act="gelu_tanh"))
+        bufs = [torch.empty_like(y) for _ in range(world)] if rank == 0 else None
+        dist.gather(y.contiguous(), gather_list=bufs, dst=0)
+        sel = np.random.default_rng(rank).choice(len(rows), 8, replace=False)
+        ref = oracle.mlp(x.float().numpy()[sel], w1.float().numpy(), w2.float().numpy(),
+                         act="gelu_tanh")
+        d = np.abs(y.numpy()[sel] - ref)
+        stats = reduce_error_stats(float(d.max()), float(d.sum()), d.size, "cpu")
+        if rank == 0:
+            torch.save({"y": torch.cat(bufs, dim=0), "stats": stats}, result_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_mlp_row_split_matches_single_process(tmp_path):
+    import oracle
+    from cs348k_fast_attention_grammar_b200.inputs import make_mlp
+    path = str(tmp_path / "mlp.pt")
+    mp.start_processes(_mlp_worker, args=(2, _free_port(), path), nprocs=2, join=True,
+                       start_method="spawn")
+    res = torch.load(path)
+    x, w1, w2 = make_mlp(MLP_CFG, "cpu")
+    single = oracle.mlp(x.float().numpy(), w1.float().numpy(), w2.float().numpy(),
+                        act="gelu_tanh")
+    assert res["y"].shape == (MLP_CFG["M"], MLP_CFG["K"])
+    np.testing.assert_array_equal(res["y"].numpy(), single)
+    assert res["stats"]["max_abs"] == 0.0 and res["stats"]["elements"] == 2 * 8 * MLP_CFG["K"]
