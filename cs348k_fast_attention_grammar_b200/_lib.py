@@ -26,11 +26,18 @@ SIGNATURES = {
     "fa_version": (_c_int, []),
     "fa_attn_fwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
                              ctypes.POINTER(_i64), _c_int, _c_float, _vp]),
+    "fa_attn_fwd_f16": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                 ctypes.POINTER(_i64), _c_int, _c_float, _vp]),
     "fa_attn_fwd_f32": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
                                  _c_float, _vp]),
+    "fa_attn_fwd_f32_batched": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
+                                         _c_int, _c_int, _c_float, _vp]),
     "fa_gemm_act": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _i64, _i64, _i64,
                              _c_int, _vp]),
+    "fa_gemm_act_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _i64, _i64, _i64,
+                                 _c_int, _vp]),
     "fa_mlp_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp]),
+    "fa_mlp_fwd_f16": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp]),
     "fa_mlp_ln_fwd": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
                                _c_float, _vp]),
     "fa_layernorm_rows": (_c_int, [_vp, _vp, _c_int, _c_int, _i64, _i64, _c_float, _vp]),

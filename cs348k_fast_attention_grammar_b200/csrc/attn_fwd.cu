@@ -181,6 +181,7 @@ struct AttnCfg {
 
 struct AttnParams {
   int B, H, S;
+  int D;                  // head dim of the tensors (<= the kernel's D; the rest is zero padding)
   int n_units_per_head;   // ceil(S / 256)
   int group_q;            // scheduling groups hold group_q or group_q + 1 pairs;
   int group_r;            // the first group_r groups hold group_q + 1
@@ -244,6 +245,34 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
+// Epilogue store of accumulator columns [col, col + 32) of one output row,
+// scaled by inv_l: fp32 (OUT_F32) or 16-bit pairs (fp16 when F16, else bf16),
+// 16-byte stores; columns >= d (a multiple of 8) are padding and not written.
+template <bool OUT_F32, bool F16>
+__device__ __forceinline__ void store_o_chunk(void* o, int64_t row_off, int col, int d,
+                                              const uint32_t (&r)[32], float inv_l) {
+  if (OUT_F32) {
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<float*>(o) + row_off + col);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (col + 4 * e < d)
+        dst[e] = make_uint4(__float_as_uint(__uint_as_float(r[4 * e]) * inv_l),
+                            __float_as_uint(__uint_as_float(r[4 * e + 1]) * inv_l),
+                            __float_as_uint(__uint_as_float(r[4 * e + 2]) * inv_l),
+                            __float_as_uint(__uint_as_float(r[4 * e + 3]) * inv_l));
+  } else {
+    uint32_t w[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      w[e] = pack_16x2<F16>(__uint_as_float(r[2 * e]) * inv_l,
+                            __uint_as_float(r[2 * e + 1]) * inv_l);
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(o) + row_off + col);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      if (col + 8 * e < d) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+  }
+}
+
 // Work unit u of the two-tile kernel: tiles_per_unit (2, or 1 for small
 // problems) 128-row Q tiles of one (batch, head) pair.  Pairs are taken in consecutive groups of
 // group_q + 1 (the first group_r groups) or group_q pairs, so the K/V of a
@@ -285,14 +314,14 @@ __device__ __forceinline__ void decode_unit(const AttnParams& p, int unit, int& 
   }
 }
 
-template <int D, bool CAUSAL, bool OUT_F32>
+template <int D, bool CAUSAL, bool OUT_F32, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using C = AttnCfg<D>;
   constexpr int kEmuMod = (D == 64) ? FA_ATTN_EMU_MOD_D64 : FA_ATTN_EMU_MOD_D128;
-  constexpr bool kPackAlu = FA_ATTN_PACK_ALU != 0;
+  constexpr bool kPackAlu = FA_ATTN_PACK_ALU != 0 && !F16;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -439,8 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 9) {
     // =================== MMA issuer ===================
     if (elect_one()) {
-      constexpr uint32_t kIdQK = idesc_bf16_f32(kBM, kBN, false, false);
-      constexpr uint32_t kIdPV = idesc_bf16_f32(kBM, D, false, true);
+      constexpr uint32_t kIdQK = idesc_f32acc(kBM, kBN, false, false, F16);
+      constexpr uint32_t kIdPV = idesc_f32acc(kBM, D, false, true, F16);
       bool ok = true;
       int it = 0;              // K/V tiles consumed, over all units (ring position)
       int pb[2] = {0, 0};      // key blocks of tile t in earlier units (P phases)
@@ -666,7 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             rs2[c & 1] = fadd2(rs2[c & 1], f2_pack(p0, p1));
           else
             rs[c & 3] += p0 + p1;
-          pk[half][cc] = kPackAlu ? pack_bf16x2_alu(p0, p1) : pack_bf16x2(p0, p1);
+          pk[half][cc] = kPackAlu ? pack_bf16x2_alu(p0, p1) : pack_16x2<F16>(p0, p1);
         }
         if (FA_ATTN_SPLIT_P && half == 0) {
           // keys 0-63 of P -> TMEM columns [0, 32); the MMA warp starts on them
@@ -702,32 +731,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         tmem_ld32_wait(tO + c * 32, o);
-        if (OUT_F32) {
-          // fp32 output (the reference's own dtype): 8 x 16-byte stores.
-          if (qi < p.S) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<float*>(p.o) + orow_off + c * 32);
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              dst[e] = make_uint4(__float_as_uint(__uint_as_float(o[4 * e]) * inv_l),
-                                  __float_as_uint(__uint_as_float(o[4 * e + 1]) * inv_l),
-                                  __float_as_uint(__uint_as_float(o[4 * e + 2]) * inv_l),
-                                  __float_as_uint(__uint_as_float(o[4 * e + 3]) * inv_l));
-          }
-        } else {
-          uint32_t w[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            w[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv_l,
-                               __uint_as_float(o[2 * e + 1]) * inv_l);
-          if (qi < p.S) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + orow_off +
-                                                  c * 32);
-            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-            dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
-            dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
-          }
-        }
+        if (qi < p.S && 32 * c < p.D)
+          store_o_chunk<OUT_F32, F16>(p.o, orow_off, 32 * c, p.D, o, inv_l);
       }
       if (t == (nt[1] > 0 ? 1 : 0) && lane == 0 && wq == 0) FA_CTA_TRACE(unit, 4, globaltimer_ns());
     }
@@ -777,11 +782,11 @@ int launch_maybe_pdl(Kern kern, int grid, int threads, int smem, cudaStream_t st
   return cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, prm) == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-template <int D, bool CAUSAL, bool OUT_F32>
+template <int D, bool CAUSAL, bool OUT_F32, bool F16>
 int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                 const AttnParams& prm, int grid, cudaStream_t stream, bool pdl) {
   using C = AttnCfg<D>;
-  auto kern = attn_fwd_kernel<D, CAUSAL, OUT_F32>;
+  auto kern = attn_fwd_kernel<D, CAUSAL, OUT_F32, F16>;
   static KernelPrep prep;
   int dev = 0;
   const int rc = prepare_kernel(prep, reinterpret_cast<const void*>(kern), C::kSmemBytes, &dev);
@@ -853,7 +858,7 @@ __device__ __forceinline__ void decode_unit_q4(const AttnParams& p, int unit, in
   }
 }
 
-template <bool CAUSAL, bool OUT_F32>
+template <bool CAUSAL, bool OUT_F32, bool F16>
 __global__ void __launch_bounds__(kQ4Threads, 1)
     attn_fwd_q4_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
@@ -991,8 +996,8 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
     // =================== MMA issuer ===================
     // Per block j, for t = 0..3: O_t += P_t(j-1) V_{j-1}, then S_t = Q_t K_j^T.
     if (elect_one()) {
-      constexpr uint32_t kIdQK = idesc_bf16_f32(kBM, kQ4BN, false, false);
-      constexpr uint32_t kIdPV = idesc_bf16_f32(kBM, D, false, true);
+      constexpr uint32_t kIdQK = idesc_f32acc(kBM, kQ4BN, false, false, F16);
+      constexpr uint32_t kIdPV = idesc_f32acc(kBM, D, false, true, F16);
       bool ok = true;
       int it = 0;                     // K/V blocks consumed, over all units
       int pb[kNT] = {0, 0, 0, 0};     // blocks of tile t in earlier units (P phases)
@@ -1176,7 +1181,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
             p1 = ex2_approx(x1);
           }
           rs2[c & 1] = fadd2(rs2[c & 1], f2_pack(p0, p1));
-          pk[c] = pack_bf16x2(p0, p1);
+          pk[c] = pack_16x2<F16>(p0, p1);
         }
         tmem_st16(tS + 16 * ch, pk);
       }
@@ -1198,29 +1203,8 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
       for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
         tmem_ld32_wait(tO + c * 32, o);
-        if (qi < p.S) {
-          if (OUT_F32) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<float*>(p.o) + orow_off + c * 32);
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              dst[e] = make_uint4(__float_as_uint(__uint_as_float(o[4 * e]) * inv_l),
-                                  __float_as_uint(__uint_as_float(o[4 * e + 1]) * inv_l),
-                                  __float_as_uint(__uint_as_float(o[4 * e + 2]) * inv_l),
-                                  __float_as_uint(__uint_as_float(o[4 * e + 3]) * inv_l));
-          } else {
-            uint32_t w[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-              w[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv_l,
-                                 __uint_as_float(o[2 * e + 1]) * inv_l);
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + orow_off +
-                                                  c * 32);
-            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-            dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
-            dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
-          }
-        }
+        if (qi < p.S && 32 * c < p.D)
+          store_o_chunk<OUT_F32, F16>(p.o, orow_off, 32 * c, p.D, o, inv_l);
       }
     }
     if (my_nt > 0) ++ou;
@@ -1243,11 +1227,11 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
   }
 }
 
-template <bool CAUSAL, bool OUT_F32>
+template <bool CAUSAL, bool OUT_F32, bool F16>
 int launch_attn_q4(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                    const AttnParams& prm, int grid, cudaStream_t stream, bool pdl) {
   using C = AttnQ4Cfg;
-  auto kern = attn_fwd_q4_kernel<CAUSAL, OUT_F32>;
+  auto kern = attn_fwd_q4_kernel<CAUSAL, OUT_F32, F16>;
   static KernelPrep prep;
   int dev = 0;
   const int rc = prepare_kernel(prep, reinterpret_cast<const void*>(kern), C::kSmemBytes, &dev);
@@ -1307,13 +1291,14 @@ namespace {
 // Shared host path of fa_attn_fwd / fa_attn_fwd_f32 (arguments already
 // validated): tensor maps, scheduling groups, launch.
 int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D,
-             const int64_t* st, int causal, float scale, bool out_f32, cudaStream_t stream,
-             bool pdl = false) {
+             const int64_t* st, int causal, float scale, bool out_f32, bool f16,
+             cudaStream_t stream, bool pdl = false) {
   int dev = 0;
   int rc = prepare_device(nullptr, 0, &dev);
   if (rc != FA_OK) return rc;
-  // D = 64: four-tile kernel with 64-key blocks; D = 128: two-tile kernel.
-  const bool q4 = (D == 64);
+  // D <= 64: four-tile kernel with 64-key blocks; D <= 128: two-tile kernel.
+  // Head dims below the kernel's width are zero-padded by the tensor maps.
+  const bool q4 = (D <= 64);
   const int kv_rows = q4 ? kQ4BN : kBN;                  // keys per K/V block
   // Tiles per work unit: the kernel's width, halved while at most half the
   // SMs would get a unit (small problems spread over more SMs; a unit's
@@ -1325,14 +1310,17 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
     tpu /= 2;
   const int unit_rows = tpu * kBM;                         // query rows per unit
   CUtensorMap mq, mk, mv;
-  if ((rc = make_tmap_bhsd(&mq, q, B, H, S, D, st[0], st[1], st[2], kBM)) != FA_OK) return rc;
-  if ((rc = make_tmap_bhsd(&mk, k, B, H, S, D, st[4], st[5], st[6], kv_rows)) != FA_OK) return rc;
-  if ((rc = make_tmap_bhsd(&mv, v, B, H, S, D, st[8], st[9], st[10], kv_rows)) != FA_OK) return rc;
+  if ((rc = make_tmap_bhsd(&mq, q, B, H, S, D, st[0], st[1], st[2], kBM, f16)) != FA_OK) return rc;
+  if ((rc = make_tmap_bhsd(&mk, k, B, H, S, D, st[4], st[5], st[6], kv_rows, f16)) != FA_OK)
+    return rc;
+  if ((rc = make_tmap_bhsd(&mv, v, B, H, S, D, st[8], st[9], st[10], kv_rows, f16)) != FA_OK)
+    return rc;
 
   AttnParams prm;
   prm.B = B;
   prm.H = H;
   prm.S = S;
+  prm.D = D;
   prm.n_units_per_head = (S + unit_rows - 1) / unit_rows;
   // Groups: at most FA_ATTN_GROUP_MIB of K/V each (>= 1 pair), the pairs
   // split as evenly as possible over them, since a short last group starts its
@@ -1367,16 +1355,22 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
   }
   if (q4) {
     if (out_f32)
-      return causal ? launch_attn_q4<true, true>(mq, mk, mv, prm, grid, stream, pdl)
-                    : launch_attn_q4<false, true>(mq, mk, mv, prm, grid, stream, pdl);
-    return causal ? launch_attn_q4<true, false>(mq, mk, mv, prm, grid, stream, pdl)
-                  : launch_attn_q4<false, false>(mq, mk, mv, prm, grid, stream, pdl);
+      return causal ? launch_attn_q4<true, true, false>(mq, mk, mv, prm, grid, stream, pdl)
+                    : launch_attn_q4<false, true, false>(mq, mk, mv, prm, grid, stream, pdl);
+    if (f16)
+      return causal ? launch_attn_q4<true, false, true>(mq, mk, mv, prm, grid, stream, pdl)
+                    : launch_attn_q4<false, false, true>(mq, mk, mv, prm, grid, stream, pdl);
+    return causal ? launch_attn_q4<true, false, false>(mq, mk, mv, prm, grid, stream, pdl)
+                  : launch_attn_q4<false, false, false>(mq, mk, mv, prm, grid, stream, pdl);
   }
   if (out_f32)
-    return causal ? launch_attn<128, true, true>(mq, mk, mv, prm, grid, stream, pdl)
-                  : launch_attn<128, false, true>(mq, mk, mv, prm, grid, stream, pdl);
-  return causal ? launch_attn<128, true, false>(mq, mk, mv, prm, grid, stream, pdl)
-                : launch_attn<128, false, false>(mq, mk, mv, prm, grid, stream, pdl);
+    return causal ? launch_attn<128, true, true, false>(mq, mk, mv, prm, grid, stream, pdl)
+                  : launch_attn<128, false, true, false>(mq, mk, mv, prm, grid, stream, pdl);
+  if (f16)
+    return causal ? launch_attn<128, true, false, true>(mq, mk, mv, prm, grid, stream, pdl)
+                  : launch_attn<128, false, false, true>(mq, mk, mv, prm, grid, stream, pdl);
+  return causal ? launch_attn<128, true, false, false>(mq, mk, mv, prm, grid, stream, pdl)
+                : launch_attn<128, false, false, false>(mq, mk, mv, prm, grid, stream, pdl);
 }
 
 // fp32 -> bf16 staging of the reference's 2-D operands into the workspace
@@ -1385,8 +1379,8 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
 // through shared memory so reads and writes both stay coalesced).
 __global__ void __launch_bounds__(256)
     stage_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
-                     const float* __restrict__ v, __nv_bfloat16* __restrict__ ws, int N, int D,
-                     int k_transposed) {
+                     const float* __restrict__ v, __nv_bfloat16* __restrict__ ws, int64_t N,
+                     int D, int k_transposed) {
   __shared__ float tile[32][33];
   // The attention kernel may start its set-up now; its loads wait for this
   // grid to complete.
@@ -1394,7 +1388,7 @@ __global__ void __launch_bounds__(256)
   const int z = blockIdx.z;
   const float* src = (z == 0) ? q : (z == 1) ? k : v;
   __nv_bfloat16* dst = ws + static_cast<int64_t>(z) * N * D;
-  const int n0 = blockIdx.x * 32;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 32;
   const int d0 = blockIdx.y * 32;
   const int tx = threadIdx.x & 31;
   const int ty = threadIdx.x >> 5;   // 0..7
@@ -1402,20 +1396,21 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int r = ty; r < 32; r += 8) {      // r = d within the tile, read along n
       const int d = d0 + r, n = n0 + tx;
-      tile[r][tx] = (n < N) ? src[static_cast<int64_t>(d) * N + n] : 0.f;
+      tile[r][tx] = (n < N && d < D) ? src[static_cast<int64_t>(d) * N + n] : 0.f;
     }
     __syncthreads();
 #pragma unroll
     for (int r = ty; r < 32; r += 8) {      // r = n within the tile, write along d
       const int n = n0 + r;
-      if (n < N) dst[static_cast<int64_t>(n) * D + d0 + tx] = __float2bfloat16_rn(tile[tx][r]);
+      if (n < N && d0 + tx < D)
+        dst[static_cast<int64_t>(n) * D + d0 + tx] = __float2bfloat16_rn(tile[tx][r]);
     }
   } else {
 #pragma unroll
     for (int r = ty; r < 32; r += 8) {
-      const int n = n0 + r;
-      if (n < N) {
-        const int64_t i = static_cast<int64_t>(n) * D + d0 + tx;
+      const int64_t n = static_cast<int64_t>(n0) + r;
+      if (n < N && d0 + tx < D) {
+        const int64_t i = n * D + d0 + tx;
         dst[i] = __float2bfloat16_rn(src[i]);
       }
     }
@@ -1459,13 +1454,17 @@ extern "C" int fa_selftest_exp2(const float* x, float* out, int n, void* stream)
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int H,
-                           int S, int D, const int64_t* st, int causal, float scale,
-                           void* stream) {
-  using namespace fa;
+namespace fa {
+namespace {
+
+bool head_dim_ok(int D) { return D >= 8 && D <= 128 && (D % 8) == 0; }
+
+// Argument checks shared by fa_attn_fwd and fa_attn_fwd_f16 (no CUDA call).
+int check_attn_args(const void* q, const void* k, const void* v, const void* o, int B, int H,
+                    int S, int D, const int64_t* st) {
   if (!q || !k || !v || !o || !st) return FA_ERR_NULL;
   if (B <= 0 || H <= 0 || S <= 0) return FA_ERR_SHAPE;
-  if (D != 64 && D != 128) return FA_ERR_HEAD_DIM;
+  if (!head_dim_ok(D)) return FA_ERR_HEAD_DIM;
   const int64_t units = static_cast<int64_t>(B) * H * ((S + kBM - 1) / kBM);
   if (units > 0x7fffffffLL) return FA_ERR_SHAPE;
   for (int t = 0; t < 4; ++t) {
@@ -1476,7 +1475,49 @@ extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o,
   const void* ptrs[4] = {q, k, v, o};
   for (int t = 0; t < 4; ++t)
     if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 != 0) return FA_ERR_ALIGN;
-  return run_attn(q, k, v, o, B, H, S, D, st, causal, scale, false,
+  return FA_OK;
+}
+
+// fp32 -> bf16 staging of n_rows rows of D values per tensor into ws, then the
+// attention with an fp32 epilogue, launched as a programmatic dependent.
+int run_attn_f32(const void* q, const void* k, const void* v, void* o, void* ws, int B, int H,
+                 int S, int D, int k_transposed, int causal, float scale, cudaStream_t s) {
+  int dev = 0;
+  int rc = prepare_device(nullptr, 0, &dev);
+  if (rc != FA_OK) return rc;
+  __nv_bfloat16* wb = static_cast<__nv_bfloat16*>(ws);
+  const int64_t rows = static_cast<int64_t>(B) * H * S;
+  const dim3 grid(static_cast<unsigned>((rows + 31) / 32), (D + 31) / 32, 3);
+  stage_f32_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(q),
+                                       static_cast<const float*>(k),
+                                       static_cast<const float*>(v), wb, rows, D, k_transposed);
+  if (cudaGetLastError() != cudaSuccess) return FA_ERR_LAUNCH;
+  const int64_t sd = static_cast<int64_t>(S) * D, hsd = sd * H, n = hsd * B;
+  const int64_t st[16] = {hsd, sd, D, 1, hsd, sd, D, 1, hsd, sd, D, 1, hsd, sd, D, 1};
+  return run_attn(wb, wb + n, wb + 2 * n, o, B, H, S, D, st, causal, scale, true, false, s,
+                  /*pdl=*/true);
+}
+
+}  // namespace
+}  // namespace fa
+
+extern "C" int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int H,
+                           int S, int D, const int64_t* st, int causal, float scale,
+                           void* stream) {
+  using namespace fa;
+  const int rc = check_attn_args(q, k, v, o, B, H, S, D, st);
+  if (rc != FA_OK) return rc;
+  return run_attn(q, k, v, o, B, H, S, D, st, causal, scale, false, false,
+                  static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fa_attn_fwd_f16(const void* q, const void* k, const void* v, void* o, int B,
+                               int H, int S, int D, const int64_t* st, int causal, float scale,
+                               void* stream) {
+  using namespace fa;
+  const int rc = check_attn_args(q, k, v, o, B, H, S, D, st);
+  if (rc != FA_OK) return rc;
+  return run_attn(q, k, v, o, B, H, S, D, st, causal, scale, false, true,
                   static_cast<cudaStream_t>(stream));
 }
 
@@ -1486,23 +1527,29 @@ extern "C" int fa_attn_fwd_f32(const void* q, const void* k, const void* v, void
   using namespace fa;
   if (!q || !k || !v || !o || !ws) return FA_ERR_NULL;
   if (N <= 0 || (k_transposed != 0 && k_transposed != 1)) return FA_ERR_SHAPE;
-  if (D != 64 && D != 128) return FA_ERR_HEAD_DIM;
+  if (!head_dim_ok(D)) return FA_ERR_HEAD_DIM;
   if (static_cast<int64_t>(N) * D > (1ll << 28)) return FA_ERR_SHAPE;
   const void* ptrs[5] = {q, k, v, o, ws};
   for (int t = 0; t < 5; ++t)
     if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 != 0) return FA_ERR_ALIGN;
-  int dev = 0;
-  int rc = prepare_device(nullptr, 0, &dev);
-  if (rc != FA_OK) return rc;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  __nv_bfloat16* wb = static_cast<__nv_bfloat16*>(ws);
-  const dim3 grid((N + 31) / 32, D / 32, 3);
-  stage_f32_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(q),
-                                       static_cast<const float*>(k),
-                                       static_cast<const float*>(v), wb, N, D, k_transposed);
-  if (cudaGetLastError() != cudaSuccess) return FA_ERR_LAUNCH;
-  const int64_t nd = static_cast<int64_t>(N) * D;
-  const int64_t st[16] = {nd, nd, D, 1, nd, nd, D, 1, nd, nd, D, 1, nd, nd, D, 1};
-  return run_attn(wb, wb + nd, wb + 2 * nd, o, 1, 1, N, D, st, causal, scale, true, s,
-                  /*pdl=*/true);
+  return run_attn_f32(q, k, v, o, ws, 1, 1, N, D, k_transposed, causal, scale,
+                      static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fa_attn_fwd_f32_batched(const void* q, const void* k, const void* v, void* o,
+                                       void* ws, int B, int H, int S, int D, int causal,
+                                       float scale, void* stream) {
+  using namespace fa;
+  if (!q || !k || !v || !o || !ws) return FA_ERR_NULL;
+  if (B <= 0 || H <= 0 || S <= 0) return FA_ERR_SHAPE;
+  if (!head_dim_ok(D)) return FA_ERR_HEAD_DIM;
+  const int64_t rows = static_cast<int64_t>(B) * H * S;
+  if (rows * D > (1ll << 34) || (rows + 31) / 32 > 0x7fffffffLL ||
+      static_cast<int64_t>(B) * H * ((S + kBM - 1) / kBM) > 0x7fffffffLL)
+    return FA_ERR_SHAPE;
+  const void* ptrs[5] = {q, k, v, o, ws};
+  for (int t = 0; t < 5; ++t)
+    if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 != 0) return FA_ERR_ALIGN;
+  return run_attn_f32(q, k, v, o, ws, B, H, S, D, 0, causal, scale,
+                      static_cast<cudaStream_t>(stream));
 }

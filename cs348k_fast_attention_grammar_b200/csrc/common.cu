@@ -96,14 +96,15 @@ int* device_status_ptr() {
 }
 
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                 uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols) {
+                 uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols, bool f16) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (enc == nullptr) return FA_ERR_DRIVER;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {row_stride_elems * 2};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+  CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   2, const_cast<void*>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -111,7 +112,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t col
 }
 
 int make_tmap_bhsd(CUtensorMap* map, const void* base, int B, int H, int S, int D, int64_t sb,
-                   int64_t sh, int64_t ss, uint32_t box_rows) {
+                   int64_t sh, int64_t ss, uint32_t box_rows, bool f16) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (enc == nullptr) return FA_ERR_DRIVER;
   // A size-1 dimension's stride is never used to address memory; give it a
@@ -122,7 +123,8 @@ int make_tmap_bhsd(CUtensorMap* map, const void* base, int B, int H, int S, int 
   cuuint64_t strides[3] = {(cuuint64_t)ss * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
   cuuint32_t box[4] = {64, box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+  CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   4, const_cast<void*>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -169,7 +171,8 @@ extern "C" const char* fa_strerror(int status) {
     case FA_OK: return "success";
     case FA_ERR_NULL: return "a required pointer is NULL";
     case FA_ERR_SHAPE: return "invalid shape: every dimension must be positive and in range";
-    case FA_ERR_HEAD_DIM: return "unsupported head dimension (attention supports D = 64 or 128)";
+    case FA_ERR_HEAD_DIM:
+      return "unsupported head dimension (attention supports D = 8 .. 128 in steps of 8)";
     case FA_ERR_ALIGN: return "pointer or stride is not 16-byte aligned (TMA requirement)";
     case FA_ERR_STRIDE: return "innermost stride must be 1 (contiguous last dimension)";
     case FA_ERR_TMA: return "cuTensorMapEncodeTiled rejected the tensor layout";

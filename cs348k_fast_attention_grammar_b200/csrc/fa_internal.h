@@ -38,14 +38,18 @@ int sm_count(int dev);
 // Device-global status word written by kernels (fa::kDevTimeout ...).
 int* device_status_ptr();
 
-// bf16 tensor map over a row-major [rows, cols] matrix (cols contiguous,
-// row stride in elements), box = box_rows x 64 columns, 128B swizzle.
+// Tensor map of 16-bit elements (bf16, or fp16 when f16) over a row-major
+// [rows, cols] matrix (cols contiguous, row stride in elements), box =
+// box_rows x 64 columns, 128B swizzle.
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                 uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols);
+                 uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_cols,
+                 bool f16 = false);
 
-// bf16 tensor map over a [B, H, S, D] tensor with element strides
-// (sb, sh, ss, 1): dims listed innermost first (D, S, H, B), box 64 x box_rows.
+// Tensor map of 16-bit elements over a [B, H, S, D] tensor with element
+// strides (sb, sh, ss, 1): dims listed innermost first (D, S, H, B), box
+// 64 x box_rows.  D may be below 64 (or between 64 and 128 for two boxes side
+// by side): box columns past D read as zeros.
 int make_tmap_bhsd(CUtensorMap* map, const void* base, int B, int H, int S, int D,
-                   int64_t sb, int64_t sh, int64_t ss, uint32_t box_rows);
+                   int64_t sb, int64_t sh, int64_t ss, uint32_t box_rows, bool f16 = false);
 
 }  // namespace fa

@@ -89,9 +89,10 @@ __device__ __forceinline__ float apply_act(float x, int act) {
   return x;
 }
 
-// Epilogue of 32 accumulator columns of one row: activation, optional bf16
-// residual (added in fp32), bf16 pack, 16-byte stores; rows >= M and columns
-// >= N (N is a multiple of 32) are skipped.
+// Epilogue of 32 accumulator columns of one row: activation, optional
+// residual (added in fp32), 16-bit pack (fp16 when F16, else bf16), 16-byte
+// stores; rows >= M and columns >= N (N is a multiple of 32) are skipped.
+template <bool F16>
 __device__ __forceinline__ void store_chunk(const GemmParams& p, int row, int col,
                                             const uint32_t (&r)[32]) {
   float v[32];
@@ -106,14 +107,14 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, int row, int co
       const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        v[8 * q + 2 * e] += __uint_as_float(ws[e] << 16);
-        v[8 * q + 2 * e + 1] += __uint_as_float(ws[e] & 0xffff0000u);
+        v[8 * q + 2 * e] += unpack_16<F16>(ws[e], false);
+        v[8 * q + 2 * e + 1] += unpack_16<F16>(ws[e], true);
       }
     }
   }
   uint32_t w[16];
 #pragma unroll
-  for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+  for (int e = 0; e < 16; ++e) w[e] = pack_16x2<F16>(v[2 * e], v[2 * e + 1]);
   if (in) {
     uint4* dst = reinterpret_cast<uint4*>(p.c + static_cast<int64_t>(row) * p.ldc + col);
     dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -123,6 +124,7 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, int row, int co
   }
 }
 
+template <bool F16>
 __global__ void __launch_bounds__(kGThreads, 1)
     gemm_act_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
@@ -203,7 +205,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
   } else if (warp == 1) {
     // =================== MMA issuer ===================
     if (elect_one()) {
-      constexpr uint32_t kId = idesc_bf16_f32(kGBM, kGBN, false, true);
+      constexpr uint32_t kId = idesc_f32acc(kGBM, kGBN, false, true, F16);
       int it = 0, tcount = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++tcount) {
@@ -257,7 +259,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
       for (int c = 0; c < kGBN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32_wait(tmem + lane_off + 256u * acc + c * 32, r);
-        store_chunk(p, row, tn * kGBN + c * 32, r);
+        store_chunk<F16>(p, row, tn * kGBN + c * 32, r);
       }
       tc_fence_before();
       mbar_arrive(bar_acc_empty(acc));
@@ -297,6 +299,7 @@ constexpr int kG2NumBars = 2 * kG2Stages + 4 + 1;  // full, empty, acc_full[2], 
 constexpr int kG2MiscOff = kG2BarOff + kG2NumBars * 8;
 constexpr int kG2SmemBytes = kG2MiscOff + 16 + 1024;
 
+template <bool F16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
     gemm_act_2sm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
@@ -381,7 +384,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
   } else if (warp == 1) {
     // =================== MMA issuer (rank 0) ===================
     if (rank == 0 && elect_one()) {
-      constexpr uint32_t kId = idesc_bf16_f32(kG2BM, kG2BN, false, true);
+      constexpr uint32_t kId = idesc_f32acc(kG2BM, kG2BN, false, true, F16);
       int it = 0, tcount = 0;
       bool ok = true;
       for (int tile = first_tile; ok && tile < p.num_tiles; tile += tile_step, ++tcount) {
@@ -433,7 +436,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
       for (int c = 0; c < kG2BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32_wait(tmem + lane_off + 256u * acc + c * 32, r);
-        store_chunk(p, row, tn * kG2BN + c * 32, r);
+        store_chunk<F16>(p, row, tn * kG2BN + c * 32, r);
       }
       tc_fence_before();
       __syncwarp();
@@ -450,51 +453,57 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGThreads, 1)
   }
 }
 
-KernelPrep g_gemm_prep;
+KernelPrep g_gemm_prep[2];                     // gemm_act_kernel<bf16 / fp16>
 std::mutex g_clusters_mu;
-std::atomic<int> g_clusters_2sm[64] = {};   // co-resident clusters of gemm_act_2sm_kernel
+std::atomic<int> g_clusters_2sm[2][64] = {};   // co-resident clusters of gemm_act_2sm_kernel
 
-// Set-up of the two-SM kernel on device dev (once): shared-memory limit and
-// the number of clusters that fit on the device at once.
+// Set-up of the two-SM kernel on device dev (once per element type): shared
+// memory limit and the number of clusters that fit on the device at once.
+template <bool F16>
 int clusters_2sm(int dev, int* n_out) {
-  int n = g_clusters_2sm[dev].load(std::memory_order_acquire);
+  std::atomic<int>& slot = g_clusters_2sm[F16 ? 1 : 0][dev];
+  int n = slot.load(std::memory_order_acquire);
   if (n > 0) {
     *n_out = n;
     return FA_OK;
   }
   std::lock_guard<std::mutex> lk(g_clusters_mu);
-  n = g_clusters_2sm[dev].load(std::memory_order_relaxed);
+  n = slot.load(std::memory_order_relaxed);
   if (n == 0) {
-    if (cudaFuncSetAttribute(gemm_act_2sm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kG2SmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_act_2sm_kernel<F16>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kG2SmemBytes) !=
+        cudaSuccess)
       return FA_ERR_CUDA;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74);
     cfg.blockDim = dim3(kGThreads);
     cfg.dynamicSmemBytes = kG2SmemBytes;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_act_2sm_kernel, &cfg) != cudaSuccess || n <= 0)
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_act_2sm_kernel<F16>, &cfg) != cudaSuccess ||
+        n <= 0)
       n = (sm_count(dev) > 0 ? sm_count(dev) : 148) / 2;
     (void)cudaGetLastError();
-    g_clusters_2sm[dev].store(n, std::memory_order_release);
+    slot.store(n, std::memory_order_release);
   }
   *n_out = n;
   return FA_OK;
 }
 
+// C = act(A B) (+ residual) with 16-bit operands: bf16, or fp16 when f16.
 int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int64_t lda,
                 int64_t ldb, int64_t ldc, int act, cudaStream_t stream,
-                const void* res = nullptr, int64_t ldr = 0) {
+                const void* res = nullptr, int64_t ldr = 0, bool f16 = false) {
   int dev = 0;
   {
-    const int rc = prepare_kernel(g_gemm_prep, reinterpret_cast<const void*>(gemm_act_kernel),
-                                  kGSmemBytes, &dev);
+    const void* kern = f16 ? reinterpret_cast<const void*>(gemm_act_kernel<true>)
+                           : reinterpret_cast<const void*>(gemm_act_kernel<false>);
+    const int rc = prepare_kernel(g_gemm_prep[f16 ? 1 : 0], kern, kGSmemBytes, &dev);
     if (rc != FA_OK) return rc;
   }
   const int num_sms = sm_count(dev);
   CUtensorMap ma, mb;
-  int rc = make_tmap_2d(&ma, a, M, K, lda, kGBM, 64);
+  int rc = make_tmap_2d(&ma, a, M, K, lda, kGBM, 64, f16);
   if (rc != FA_OK) return rc;
-  rc = make_tmap_2d(&mb, b, K, N, ldb, 64, 64);
+  rc = make_tmap_2d(&mb, b, K, N, ldb, 64, 64, f16);
   if (rc != FA_OK) return rc;
   GemmParams p;
   p.M = M;
@@ -526,13 +535,21 @@ int launch_gemm(const void* a, const void* b, void* c, int M, int N, int K, int6
   if (p.status == nullptr) return FA_ERR_CUDA;
   if (two_sm) {
     int clusters = 0;
-    if ((rc = clusters_2sm(dev, &clusters)) != FA_OK) return rc;
+    if ((rc = f16 ? clusters_2sm<true>(dev, &clusters) : clusters_2sm<false>(dev, &clusters)) !=
+        FA_OK)
+      return rc;
     const int grid = 2 * min(p.num_tiles, clusters);
-    gemm_act_2sm_kernel<<<grid, kGThreads, kG2SmemBytes, stream>>>(ma, mb, p);
+    if (f16)
+      gemm_act_2sm_kernel<true><<<grid, kGThreads, kG2SmemBytes, stream>>>(ma, mb, p);
+    else
+      gemm_act_2sm_kernel<false><<<grid, kGThreads, kG2SmemBytes, stream>>>(ma, mb, p);
     return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
   }
   const int grid = min(p.num_tiles, num_sms > 0 ? num_sms : 148);
-  gemm_act_kernel<<<grid, kGThreads, kGSmemBytes, stream>>>(ma, mb, p);
+  if (f16)
+    gemm_act_kernel<true><<<grid, kGThreads, kGSmemBytes, stream>>>(ma, mb, p);
+  else
+    gemm_act_kernel<false><<<grid, kGThreads, kGSmemBytes, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
@@ -769,4 +786,29 @@ extern "C" int fa_mlp_fwd(const void* x, const void* w1, const void* w2, void* h
   rc = fa::launch_gemm(x, w1, hidden, M, N, K, K, N, N, act, s);
   if (rc != FA_OK) return rc;
   return fa::launch_gemm(hidden, w2, y, M, K, N, N, K, K, FA_ACT_NONE, s);
+}
+
+// ---------------------------------------------------------------------------
+// fp16 variants of fa_gemm_act / fa_mlp_fwd: the same kernels instantiated
+// with fp16 operands (kind::f16, A/B format f16), fp32 accumulation, fp16
+// outputs.
+// ---------------------------------------------------------------------------
+extern "C" int fa_gemm_act_f16(const void* a, const void* b, void* c, int M, int N, int K,
+                               int64_t lda, int64_t ldb, int64_t ldc, int act, void* stream) {
+  int rc = fa::check_gemm_args(a, b, c, M, N, K, lda, ldb, ldc, act);
+  if (rc != FA_OK) return rc;
+  return fa::launch_gemm(a, b, c, M, N, K, lda, ldb, ldc, act,
+                         static_cast<cudaStream_t>(stream), nullptr, 0, /*f16=*/true);
+}
+
+extern "C" int fa_mlp_fwd_f16(const void* x, const void* w1, const void* w2, void* hidden,
+                              void* y, int M, int K, int N, int act, void* stream) {
+  int rc = fa::check_gemm_args(x, w1, hidden, M, N, K, K, N, N, act);
+  if (rc != FA_OK) return rc;
+  rc = fa::check_gemm_args(hidden, w2, y, M, K, N, N, K, K, FA_ACT_NONE);
+  if (rc != FA_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = fa::launch_gemm(x, w1, hidden, M, N, K, K, N, N, act, s, nullptr, 0, true);
+  if (rc != FA_OK) return rc;
+  return fa::launch_gemm(hidden, w2, y, M, K, N, N, K, K, FA_ACT_NONE, s, nullptr, 0, true);
 }

@@ -305,15 +305,19 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
-// Instruction descriptor, kind::f16 with bf16 A/B and fp32 accumulate.
-//   [4,6) D format (1 = f32), [7,10) A format (1 = bf16), [10,13) B format,
-//   [15] A major (0 = K), [16] B major (0 = K, 1 = MN), [17,23) N >> 3,
-//   [24,29) M >> 4.
+// Instruction descriptor, kind::f16 with 16-bit A/B and fp32 accumulate.
+//   [4,6) D format (1 = f32), [7,10) A format (0 = f16, 1 = bf16), [10,13) B
+//   format (A and B always the same type here), [15] A major (0 = K), [16] B
+//   major (0 = K, 1 = MN), [17,23) N >> 3, [24,29) M >> 4.
+__host__ __device__ constexpr uint32_t idesc_f32acc(int M, int N, bool a_mn_major,
+                                                    bool b_mn_major, bool f16) {
+  return (1u << 4) | ((f16 ? 0u : 1u) << 7) | ((f16 ? 0u : 1u) << 10) |
+         ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_major,
                                                       bool b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
-         ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
-         (static_cast<uint32_t>(M >> 4) << 24);
+  return idesc_f32acc(M, N, a_mn_major, b_mn_major, false);
 }
 
 // ----------------------------------------------------------------------------
@@ -334,6 +338,29 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// Two fp32 -> one f16x2 word: low half = lo, high half = hi (round to nearest even).
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// The 16-bit element type of a kernel instantiation: fp16 when F16, else bf16.
+template <bool F16>
+__device__ __forceinline__ uint32_t pack_16x2(float lo, float hi) {
+  return F16 ? pack_f16x2(lo, hi) : pack_bf16x2(lo, hi);
+}
+// One 16-bit element (low half of w when hi is false) as fp32.
+template <bool F16>
+__device__ __forceinline__ float unpack_16(uint32_t w, bool hi) {
+  if (F16) {
+    const unsigned short h = static_cast<unsigned short>(hi ? (w >> 16) : (w & 0xffffu));
+    float f;
+    asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+    return f;
+  }
+  return __uint_as_float(hi ? (w & 0xffff0000u) : (w << 16));
 }
 
 // Paired fp32 arithmetic (two lanes of fp32 in one 64-bit register pair).

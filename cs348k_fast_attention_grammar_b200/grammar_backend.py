@@ -358,8 +358,8 @@ def _check_shapes(kind: str, roles: dict, tensors: dict, params: dict) -> None:
         (n, d), (d2, n2), (n3, d3) = shp["q"], shp["kt"], shp["v"]
         if not (d == d2 and n == n2 == n3 and d == d3):
             raise UnsupportedProgram(f"attention shapes {shp} are not Q[N,d] KT[d,N] V[N,d]")
-        if d not in (64, 128):
-            raise UnsupportedProgram(f"head dim {d} (the kernel takes 64 or 128)")
+        if not (8 <= d <= 128 and d % 8 == 0):
+            raise UnsupportedProgram(f"head dim {d} (the kernels take 8 .. 128, multiples of 8)")
     elif kind in ("mlp", "mlp_ln"):
         (m, k), (k2, n), (n2, k3) = shp["x"], shp["w1"], shp["w2"]
         if not (k == k2 == k3 and n == n2) or k % 64 or n % 64:

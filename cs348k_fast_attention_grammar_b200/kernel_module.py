@@ -6,9 +6,11 @@ kernels, so the reference's own harness can time this library unmodified::
 A module exposes ``fn(*inputs) -> output`` with inputs in sorted tensor-name
 order (``grammar/kernel_ast.py:673``) and ``KERNEL_META`` (``:1280-1287``).
 The reference's arrays are DLPack-capable (cupy); they are wrapped with
-``torch.from_dlpack`` as ``pytorch-naive.py:36-38`` does, cast to bf16 for the
-tensor cores (fp32 accumulate), and the result is returned in the input dtype.
-As in the reference, the callee allocates and returns the output.
+``torch.from_dlpack`` as ``pytorch-naive.py:36-38`` does.  fp16 and bf16
+arrays run the tensor cores in their own type (fp32 accumulate); fp32 arrays
+(the reference's default) are staged to bf16 on the device in the same C
+call, with an fp32 result.  As in the reference, the callee allocates and
+returns the output.
 """
 
 from __future__ import annotations
@@ -45,27 +47,19 @@ def fn(KT, Q, V):
     """``fn(KT, Q, V) -> O`` for ``KT [d, N]``, ``Q [N, d]``, ``V [N, d]``
     (the signature of ``pytorch-naive.py:23`` and every emitted module).
     fp32 inputs go through one C call (device-side bf16 staging, fp32 output);
-    bf16 inputs through the batched operator."""
+    bf16 and fp16 inputs through the batched operator, in their own type."""
     KT, Q, V = _as_torch(KT), _as_torch(Q), _as_torch(V)
     if Q.dtype == torch.float32:
         return attention_f32(Q.contiguous(), KT.contiguous(), V.contiguous(), k_transposed=True)
-    dtype = Q.dtype
-    q = Q.to(torch.bfloat16).unsqueeze(0).unsqueeze(0)
-    k = KT.t().to(torch.bfloat16).contiguous().unsqueeze(0).unsqueeze(0)
-    v = V.to(torch.bfloat16).contiguous().unsqueeze(0).unsqueeze(0)
-    o = attention(q.contiguous(), k, v, causal=False)
-    return o[0, 0].to(dtype)
+    # bf16 / fp16: K must be contiguous along d, so KT [d, N] is transposed once.
+    q = Q.contiguous().unsqueeze(0).unsqueeze(0)
+    k = KT.t().contiguous().unsqueeze(0).unsqueeze(0)
+    v = V.contiguous().unsqueeze(0).unsqueeze(0)
+    return attention(q, k, v, causal=False)[0, 0]
 
 
 def sota_fn(K, Q, V):
     """``fn(K, Q, V)`` on ``[B, H, S, D]`` tensors, the argument order of
     ``flash-attn2-sota.py:41``."""
     K, Q, V = _as_torch(K), _as_torch(Q), _as_torch(V)
-    if Q.dtype == torch.float32 and Q.shape[0] == 1 and Q.shape[1] == 1:
-        o = attention_f32(Q[0, 0].contiguous(), K[0, 0].contiguous(), V[0, 0].contiguous())
-        return o.view(Q.shape)
-    dtype = Q.dtype
-    bf = torch.bfloat16
-    o = attention(Q.to(bf).contiguous(), K.to(bf).contiguous(), V.to(bf).contiguous(),
-                  causal=False)
-    return o.to(dtype)
+    return attention(Q.contiguous(), K.contiguous(), V.contiguous(), causal=False)

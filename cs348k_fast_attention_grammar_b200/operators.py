@@ -1,6 +1,7 @@
 """Python operators over the C ABI: the drop-in for the reference's hot path.
 
-* ``attention(q, k, v, causal=False)`` on ``[B, H, S, D]`` bf16 CUDA tensors --
+* ``attention(q, k, v, causal=False)`` on ``[B, H, S, D]`` CUDA tensors (bf16,
+  fp16, or contiguous fp32 staged to bf16 on the device) --
   the operator behind the reference's kernel-module protocol (``bench.py:14-20``;
   ``pytorch-naive.py:23-65``, ``flash-attn2-sota.py:41-63``,
   ``old/kernels/old/naive.py:27-56``).
@@ -35,6 +36,8 @@ import torch
 from . import _lib
 
 _BF16 = torch.bfloat16
+_F16 = torch.float16
+_HALF_TYPES = (_BF16, _F16)
 
 
 # torch's raw current-stream accessor (the one its compiled kernels use) is
@@ -93,38 +96,50 @@ class _on_device:
             torch.cuda.set_device(self.prev)
 
 
-def _check_cuda_bf16(name: str, t: torch.Tensor) -> None:
+def _check_cuda(name: str, t: torch.Tensor, dtypes=(_BF16,)) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
     if not t.is_cuda:
         raise ValueError(f"{name} must be a CUDA tensor (got device {t.device})")
-    if t.dtype != _BF16:
-        raise TypeError(f"{name} must be bfloat16 (got {t.dtype})")
+    if t.dtype not in dtypes:
+        names = " or ".join(str(d).replace("torch.", "") for d in dtypes)
+        raise TypeError(f"{name} must be {names} (got {t.dtype})")
+
+
+def _check_cuda_bf16(name: str, t: torch.Tensor) -> None:
+    _check_cuda(name, t, (_BF16,))
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
               scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """softmax(q k^T * scale [+ causal mask]) v on ``[B, H, S, D]`` bf16 tensors.
+    """softmax(q k^T * scale [+ causal mask]) v on ``[B, H, S, D]`` CUDA tensors.
 
-    ``scale`` defaults to ``1/sqrt(D)`` (``run_attention_search.py:40``).
-    Inputs may have arbitrary batch/head/sequence strides (multiples of 8
-    elements) but must be contiguous along D.  Returns a new ``[B, H, S, D]``
-    tensor unless ``out`` is given.
+    ``scale`` defaults to ``1/sqrt(D)`` (``run_attention_search.py:40``); D is
+    8 .. 128, a multiple of 8.  bf16 and fp16 inputs (all three the same
+    type) run the tensor cores in that type with fp32 accumulation; they may
+    have arbitrary batch/head/sequence strides (multiples of 8 elements) but
+    must be contiguous along D.  fp32 inputs (the reference's dtype) must be
+    contiguous; they are staged to bf16 on the device in the same C call and
+    O is written in fp32.  Returns a new ``[B, H, S, D]`` tensor of the input
+    dtype unless ``out`` is given.
     """
     for name, t in (("q", q), ("k", k), ("v", v)):
-        _check_cuda_bf16(name, t)
+        _check_cuda(name, t, (_BF16, _F16, torch.float32))
         if t.dim() != 4:
             raise ValueError(f"{name} must be 4-D [B, H, S, D] (got {tuple(t.shape)})")
     if not (q.shape == k.shape == v.shape):
         raise ValueError(f"q, k, v shapes differ: {tuple(q.shape)}, {tuple(k.shape)}, "
                          f"{tuple(v.shape)}")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError(f"q, k, v dtypes differ: {q.dtype}, {k.dtype}, {v.dtype}")
     if not (q.device == k.device == v.device):
         raise ValueError("q, k, v must be on the same device")
     B, H, S, D = q.shape
+    dtype = q.dtype
     if out is None:
-        out = torch.empty((B, H, S, D), dtype=_BF16, device=q.device)
+        out = torch.empty((B, H, S, D), dtype=dtype, device=q.device)
     else:
-        _check_cuda_bf16("out", out)
+        _check_cuda("out", out, (dtype,))
         if tuple(out.shape) != (B, H, S, D) or out.device != q.device:
             raise ValueError("out must match q's shape and device")
     if scale is None:
@@ -132,12 +147,25 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
     if B * H * S == 0:
         return out                 # empty batch, heads or sequence: nothing to compute
     lib = _lib.load()
+    if dtype == torch.float32:
+        for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+            if not t.is_contiguous():
+                raise ValueError(f"fp32 {name} must be contiguous")
+        with _on_device(q.device):
+            stream = _stream_ptr(q.device)
+            ws = _staging_workspace(3 * q.numel(), q.device, stream)
+            rc = lib.fa_attn_fwd_f32_batched(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                             out.data_ptr(), ws.data_ptr(), B, H, S, D,
+                                             int(bool(causal)), float(scale), stream)
+        _lib.check(rc, "fa_attn_fwd_f32_batched")
+        return out
     strides = (ctypes.c_int64 * 16)(*q.stride(), *k.stride(), *v.stride(), *out.stride())
+    fn, where = ((lib.fa_attn_fwd_f16, "fa_attn_fwd_f16") if dtype == _F16
+                 else (lib.fa_attn_fwd, "fa_attn_fwd"))
     with _on_device(q.device):
-        rc = lib.fa_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-                             B, H, S, D, strides, int(bool(causal)), float(scale),
-                             _stream_ptr(q.device))
-    _lib.check(rc, "fa_attn_fwd")
+        rc = fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, H, S, D, strides,
+                int(bool(causal)), float(scale), _stream_ptr(q.device))
+    _lib.check(rc, where)
     return out
 
 
@@ -182,11 +210,12 @@ def attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
 
 def attention_bshd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                    scale: float | None = None) -> torch.Tensor:
-    """The legacy ``fn(q, k, v)`` on ``(B, S, H, D)`` tensors
-    (``old/benchmark.py:17-21``); the head/sequence transpose is expressed as
-    strides, so no data is copied.  Returns ``(B, S, H, D)``."""
+    """The legacy ``fn(q, k, v)`` on ``(B, S, H, D)`` bf16 or fp16 tensors
+    (``old/benchmark.py:17-21``, fp16 by default there); the head/sequence
+    transpose is expressed as strides, so no data is copied.  Returns
+    ``(B, S, H, D)``."""
     for name, t in (("q", q), ("k", k), ("v", v)):
-        _check_cuda_bf16(name, t)
+        _check_cuda(name, t, _HALF_TYPES)
         if t.dim() != 4:
             raise ValueError(f"{name} must be 4-D (B, S, H, D)")
     out = torch.empty_like(q, memory_format=torch.contiguous_format)
@@ -329,10 +358,10 @@ def mlp_from_host(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
 
 def gemm_act(a: torch.Tensor, b: torch.Tensor, act: str = "none",
              out: torch.Tensor | None = None) -> torch.Tensor:
-    """``act(a @ b)`` for row-major bf16 ``a [M, K]``, ``b [K, N]``; K and N
-    multiples of 64."""
-    _check_cuda_bf16("a", a)
-    _check_cuda_bf16("b", b)
+    """``act(a @ b)`` for row-major ``a [M, K]``, ``b [K, N]`` (both bf16 or
+    both fp16; the result has their dtype); K and N multiples of 64."""
+    _check_cuda("a", a, _HALF_TYPES)
+    _check_cuda("b", b, (a.dtype,))
     if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
         raise ValueError(f"bad GEMM shapes {tuple(a.shape)} @ {tuple(b.shape)}")
     if a.stride(1) != 1 or b.stride(1) != 1:
@@ -342,26 +371,30 @@ def gemm_act(a: torch.Tensor, b: torch.Tensor, act: str = "none",
     M, K = a.shape
     N = b.shape[1]
     if out is None:
-        out = torch.empty((M, N), dtype=_BF16, device=a.device)
+        out = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    else:
+        _check_cuda("out", out, (a.dtype,))
     if M == 0:
         return out                 # no rows: nothing to compute
     lib = _lib.load()
+    fn, where = ((lib.fa_gemm_act_f16, "fa_gemm_act_f16") if a.dtype == _F16
+                 else (lib.fa_gemm_act, "fa_gemm_act"))
     with _on_device(a.device):
-        rc = lib.fa_gemm_act(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
-                             a.stride(0), b.stride(0), out.stride(0),
-                             _lib.ACTIVATIONS[act], _stream_ptr(a.device))
-    _lib.check(rc, "fa_gemm_act")
+        rc = fn(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, a.stride(0), b.stride(0),
+                out.stride(0), _lib.ACTIVATIONS[act], _stream_ptr(a.device))
+    _lib.check(rc, where)
     return out
 
 
 def mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, act: str = "gelu_tanh",
         hidden: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
     """``act(x @ w1) @ w2`` with ``x [M, K]``, ``w1 [K, N]``, ``w2 [N, K]``
-    (row-major bf16, K and N multiples of 64).  ``act`` is "gelu_tanh" (the
-    benchmark block) or "relu" (``run_mlp_search.py:62-64``).  ``hidden`` is
-    the ``[M, N]`` bf16 workspace for ``act(x @ w1)``."""
+    (row-major, all bf16 or all fp16, K and N multiples of 64).  ``act`` is
+    "gelu_tanh" (the benchmark block) or "relu" (``run_mlp_search.py:62-64``).
+    ``hidden`` is the ``[M, N]`` workspace for ``act(x @ w1)``."""
+    _check_cuda("x", x, _HALF_TYPES)
     for name, t in (("x", x), ("w1", w1), ("w2", w2)):
-        _check_cuda_bf16(name, t)
+        _check_cuda(name, t, (x.dtype,))
         if t.dim() != 2 or not t.is_contiguous():
             raise ValueError(f"{name} must be a contiguous 2-D tensor")
     M, K = x.shape
@@ -372,17 +405,20 @@ def mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, act: str = "gelu_ta
     if act not in ("gelu_tanh", "relu"):
         raise ValueError("act must be 'gelu_tanh' or 'relu'")
     if hidden is None:
-        hidden = torch.empty((M, N), dtype=_BF16, device=x.device)
+        hidden = torch.empty((M, N), dtype=x.dtype, device=x.device)
     if out is None:
-        out = torch.empty((M, K), dtype=_BF16, device=x.device)
+        out = torch.empty((M, K), dtype=x.dtype, device=x.device)
+    _check_cuda("hidden", hidden, (x.dtype,))
+    _check_cuda("out", out, (x.dtype,))
     if M == 0:
         return out                 # no rows: nothing to compute
     lib = _lib.load()
+    fn, where = ((lib.fa_mlp_fwd_f16, "fa_mlp_fwd_f16") if x.dtype == _F16
+                 else (lib.fa_mlp_fwd, "fa_mlp_fwd"))
     with _on_device(x.device):
-        rc = lib.fa_mlp_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), hidden.data_ptr(),
-                            out.data_ptr(), M, K, N, _lib.ACTIVATIONS[act],
-                            _stream_ptr(x.device))
-    _lib.check(rc, "fa_mlp_fwd")
+        rc = fn(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), hidden.data_ptr(), out.data_ptr(),
+                M, K, N, _lib.ACTIVATIONS[act], _stream_ptr(x.device))
+    _lib.check(rc, where)
     return out
 
 

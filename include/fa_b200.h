@@ -5,8 +5,9 @@
  * All entry points are stream-ordered and asynchronous on the caller's
  * stream; none of them allocates device memory, and the caller owns every
  * buffer.  Every function returns an fa_status (0 = success); no C++
- * exception crosses this boundary.  Tensors are bf16 (raw 16-bit words),
- * pointers are device pointers, strides are in elements.
+ * exception crosses this boundary.  Tensors are bf16 (raw 16-bit words)
+ * unless the name says f16 or f32, pointers are device pointers, strides are
+ * in elements.
  *
  * Reference interfaces replaced (paths inside nriedman/cs348k-fast-attention-grammar):
  *   fa_attn_fwd  <- the attention operator behind the kernel-module protocol
@@ -26,6 +27,12 @@
  *                   "matmul" reduction rule grammar/kernel_ast.py:207-211
  *                   (ct.mma K-loop) followed by the relu stage of
  *                   run_mlp_search.py:62-64.
+ *   *_f16        <- the same operators at the reference harnesses' default
+ *                   dtype, fp16 (bench.py:32 DTYPE_MAP, old/benchmark.py:96
+ *                   --dtype fp16, old/kernels/old/naive.py:27-56).
+ *   fa_attn_fwd_f32_batched <- the fp32 [B, H, S, D] problem of the
+ *                   reference's seeded runs (run_attention_search.py:169-181,
+ *                   BASELINE cfg0), one call for all (batch, head) pairs.
  */
 #ifndef FA_B200_H_
 #define FA_B200_H_
@@ -40,7 +47,7 @@ typedef enum fa_status {
   FA_OK = 0,
   FA_ERR_NULL = 1,         /* a required pointer is NULL                        */
   FA_ERR_SHAPE = 2,        /* a dimension is <= 0 or too large                  */
-  FA_ERR_HEAD_DIM = 3,     /* head dim not supported (attention: 64 or 128)     */
+  FA_ERR_HEAD_DIM = 3,     /* head dim not supported (attention: 8..128, x8)    */
   FA_ERR_ALIGN = 4,        /* pointer or stride not 16-byte aligned (TMA rule)  */
   FA_ERR_STRIDE = 5,       /* innermost stride is not 1                         */
   FA_ERR_TMA = 6,          /* cuTensorMapEncodeTiled rejected the tensor        */
@@ -71,7 +78,9 @@ int fa_version(void);
  *                strides[0..3] = q (b, h, s, d), strides[4..7] = k,
  *                strides[8..11] = v, strides[12..15] = o; every d-stride must
  *                be 1 and every other stride a multiple of 8 elements.
- *   D          : 64 or 128.
+ *   D          : 8 .. 128, a multiple of 8 (D <= 64 runs the four-tile
+ *                kernel, larger D the two-tile kernel; the head dim is
+ *                zero-padded to the kernel's width on chip, never in memory).
  *   causal     : nonzero = key j visible to query i iff j <= i.
  *   scale      : softmax scale (pass 1/sqrt(D) for the reference's math).
  *   stream     : cudaStream_t (NULL = legacy default stream).
@@ -88,6 +97,14 @@ int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int
                 int D, const int64_t* strides, int causal, float scale, void* stream);
 
 /*
+ * fa_attn_fwd with fp16 Q, K, V and O (raw 16-bit words): the same kernels
+ * with fp16 tensor-core operands (P is rounded to fp16 for O += P V),
+ * fp32 accumulation and softmax.  Arguments and rules as fa_attn_fwd.
+ */
+int fa_attn_fwd_f16(const void* q, const void* k, const void* v, void* o, int B, int H, int S,
+                    int D, const int64_t* strides, int causal, float scale, void* stream);
+
+/*
  * The reference's own 2-D fp32 problem in one call (the kernel-module
  * callables fn(KT, Q, V) of pytorch-naive.py:23 and of every emitted module,
  * grammar/kernel_ast.py:1267-1287, and fn(K, Q, V) of flash-attn2-sota.py:41
@@ -96,12 +113,20 @@ int fa_attn_fwd(const void* q, const void* k, const void* v, void* o, int B, int
  *   k [N, D] fp32 (k_transposed = 0) or KT [D, N] fp32 (k_transposed = 1);
  *   ws         : bf16 workspace of 3 * N * D elements (16-byte aligned), where
  *                q, k, v are staged in bf16 (one launch) for the tensor cores;
- *   D          : 64 or 128; causal, scale, stream as for fa_attn_fwd.
+ *   D          : as for fa_attn_fwd; causal, scale, stream as for fa_attn_fwd.
  * Two launches (staging, attention); O is written in fp32 by the attention
  * epilogue.  Inputs are rounded to bf16, accumulation is fp32.
  */
 int fa_attn_fwd_f32(const void* q, const void* k, const void* v, void* o, void* ws, int N,
                     int D, int k_transposed, int causal, float scale, void* stream);
+
+/*
+ * fa_attn_fwd_f32 for batched tensors: q, k, v, o contiguous [B, H, S, D]
+ * fp32; ws a bf16 workspace of 3 * B * H * S * D elements (16-byte aligned).
+ * Staging and attention as fa_attn_fwd_f32 (two launches for all pairs).
+ */
+int fa_attn_fwd_f32_batched(const void* q, const void* k, const void* v, void* o, void* ws,
+                            int B, int H, int S, int D, int causal, float scale, void* stream);
 
 /*
  * C[M, N] = act(A[M, K] @ B[K, N]) in bf16 with fp32 accumulation.
@@ -113,6 +138,10 @@ int fa_attn_fwd_f32(const void* q, const void* k, const void* v, void* o, void* 
 int fa_gemm_act(const void* a, const void* b, void* c, int M, int N, int K, int64_t lda,
                 int64_t ldb, int64_t ldc, int act, void* stream);
 
+/* fa_gemm_act with fp16 A, B and C (fp32 accumulation).  Same rules. */
+int fa_gemm_act_f16(const void* a, const void* b, void* c, int M, int N, int K, int64_t lda,
+                    int64_t ldb, int64_t ldc, int act, void* stream);
+
 /*
  * MLP block Y[M, K] = act(X[M, K] @ W1[K, N]) @ W2[N, K]   (all row-major bf16).
  *   hidden : caller-owned [M, N] bf16 workspace that receives act(X @ W1).
@@ -121,6 +150,10 @@ int fa_gemm_act(const void* a, const void* b, void* c, int M, int N, int K, int6
  */
 int fa_mlp_fwd(const void* x, const void* w1, const void* w2, void* hidden, void* y, int M,
                int K, int N, int act, void* stream);
+
+/* fa_mlp_fwd with fp16 X, W1, W2, hidden and Y (fp32 accumulation). */
+int fa_mlp_fwd_f16(const void* x, const void* w1, const void* w2, void* hidden, void* y, int M,
+                   int K, int N, int act, void* stream);
 
 /*
  * The reference's full MLP block (run_mlp_search.py:42-127, checked by its

@@ -102,7 +102,8 @@ def main():
         ("attn_N512_d64", "attention", ras.build_attention(512, 64)),
         ("attn_N256_d128_t64_k32", "attention", ras.build_attention(256, 128, tile=64, subtile_k=32)),
         ("attn_N1024_d64_t128_k64", "attention", ras.build_attention(1024, 64, tile=128, subtile_k=64)),
-        ("attn_N128_d32", "unsupported", ras.build_attention(128, 32)),
+        ("attn_N128_d32", "attention", ras.build_attention(128, 32)),
+        ("attn_N128_d256", "unsupported", ras.build_attention(128, 256)),
         ("mlp_ln_B64_Dm64_H128", "mlp_ln", rms.build_mlp_ln(64, 64, 128)),
         ("mlp_ln_B256_Dm512_H1024_t64_k64", "mlp_ln",
          rms.build_mlp_ln(256, 512, 1024, tile=64, subtile_k=64)),

@@ -90,7 +90,7 @@ def test_attention_f32_errors():
     with pytest.raises(ValueError):
         attention_f32(q, q[:256], q)
     with pytest.raises(FaError, match="head dimension"):
-        x = torch.randn(512, 32, device=DEV)
+        x = torch.randn(512, 20, device=DEV)            # not a multiple of 8
         attention_f32(x, x, x)
 
 
@@ -142,7 +142,7 @@ def test_repeated_calls_are_deterministic():
 
 
 def test_error_codes():
-    q = _rand((1, 1, 128, 96), 1).to(DEV)
+    q = _rand((1, 1, 128, 136), 1).to(DEV)              # above the largest head dim
     with pytest.raises(FaError, match="head dimension"):
         attention(q, q, q)
     ok = _rand((1, 1, 128, 64), 2).to(DEV)
@@ -155,7 +155,9 @@ def test_error_codes():
     with pytest.raises(ValueError):
         attention(q.cpu(), q.cpu(), q.cpu())
     with pytest.raises(TypeError):
-        attention(q.float(), q.float(), q.float())
+        attention(ok.to(torch.int16), ok.to(torch.int16), ok.to(torch.int16))
+    with pytest.raises(TypeError):
+        attention(ok, ok.half(), ok)                     # mixed dtypes
 
 
 # ---------------------------------------------------------------------------

@@ -53,6 +53,13 @@ def test_cfg0_seeded_inputs():
     o = attention(*(t.to(torch.bfloat16).to(DEV) for t in (q, k, v)), causal=cfg["causal"])
     torch.cuda.synchronize()
     assert_close(o.float().cpu().numpy(), ref_b, what="cfg0 bf16 entry vs oracle")
+    # the fp32 tensors as given: one batched fp32 call (device-side staging)
+    o32 = attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=cfg["causal"])
+    torch.cuda.synchronize()
+    assert o32.dtype == torch.float32 and tuple(o32.shape) == (B, H, S, D)
+    assert_close(o32.cpu().numpy(), ref_b, what="cfg0 batched fp32 entry vs oracle")
+    assert_close(o32.cpu().numpy(), ref32, max_tol=5e-2, mean_tol=5e-3,
+                 what="cfg0 batched fp32 entry vs fp32 inputs")
     # fp32 entry point, one (batch, head) pair per call, fp32 output
     for h in range(H):
         of = attention_f32(q[0, h].to(DEV), k[0, h].to(DEV), v[0, h].to(DEV),
@@ -62,6 +69,7 @@ def test_cfg0_seeded_inputs():
         assert_close(of.cpu().numpy(), ref_b[0, h], what=f"cfg0 fp32 entry head {h}")
         assert_close(of.cpu().numpy(), ref32[0, h], max_tol=5e-2, mean_tol=5e-3,
                      what=f"cfg0 fp32 entry head {h} vs fp32 inputs")
+        assert torch.equal(of, o32[0, h])     # same staging, same kernel, per pair
 
 
 def test_cfg4_all_pairs_one_launch_seeded_subset():

@@ -57,29 +57,42 @@ def test_argument_checks_without_device():
     lib = _lib.load()
     st = (ctypes.c_int64 * 16)(*([8192, 1024, 64, 1] * 4))
     p = ctypes.c_void_p(256)
+    odd = ctypes.c_void_p(258)
     codes = _declared_status_codes()
     assert lib.fa_attn_fwd(None, p, p, p, 1, 1, 16, 64, st, 0, 0.125, None) == codes["FA_ERR_NULL"]
     assert lib.fa_attn_fwd(p, p, p, p, 0, 1, 16, 64, st, 0, 0.125, None) == codes["FA_ERR_SHAPE"]
-    assert lib.fa_attn_fwd(p, p, p, p, 1, 1, 16, 96, st, 0, 0.125, None) == \
-        codes["FA_ERR_HEAD_DIM"]
+    for bad_d in (100, 136, 0, 4):          # not a multiple of 8, or outside 8..128
+        assert lib.fa_attn_fwd(p, p, p, p, 1, 1, 16, bad_d, st, 0, 0.125, None) == \
+            codes["FA_ERR_HEAD_DIM"]
+        assert lib.fa_attn_fwd_f16(p, p, p, p, 1, 1, 16, bad_d, st, 0, 0.125, None) == \
+            codes["FA_ERR_HEAD_DIM"]
+    assert lib.fa_attn_fwd_f16(None, p, p, p, 1, 1, 16, 64, st, 0, 0.125, None) == \
+        codes["FA_ERR_NULL"]
+    b32 = lib.fa_attn_fwd_f32_batched
+    assert b32(p, p, p, p, None, 1, 4, 256, 64, 0, 0.125, None) == codes["FA_ERR_NULL"]
+    assert b32(p, p, p, p, p, 1, 0, 256, 64, 0, 0.125, None) == codes["FA_ERR_SHAPE"]
+    assert b32(p, p, p, p, p, 1, 4, 256, 72 + 4, 0, 0.125, None) == codes["FA_ERR_HEAD_DIM"]
+    assert b32(p, p, p, odd, p, 1, 4, 256, 64, 0, 0.125, None) == codes["FA_ERR_ALIGN"]
     bad = (ctypes.c_int64 * 16)(*([8192, 1024, 65, 1] * 4))
     assert lib.fa_attn_fwd(p, p, p, p, 1, 1, 16, 64, bad, 0, 0.125, None) == codes["FA_ERR_ALIGN"]
     bad = (ctypes.c_int64 * 16)(*([8192, 1024, 64, 2] * 4))
     assert lib.fa_attn_fwd(p, p, p, p, 1, 1, 16, 64, bad, 0, 0.125, None) == \
         codes["FA_ERR_STRIDE"]
-    odd = ctypes.c_void_p(258)
     assert lib.fa_attn_fwd(odd, p, p, p, 1, 1, 16, 64, st, 0, 0.125, None) == \
         codes["FA_ERR_ALIGN"]
     f32 = lib.fa_attn_fwd_f32
     assert f32(p, p, p, p, None, 512, 64, 1, 0, 0.125, None) == codes["FA_ERR_NULL"]
     assert f32(p, p, p, p, p, 0, 64, 1, 0, 0.125, None) == codes["FA_ERR_SHAPE"]
     assert f32(p, p, p, p, p, 512, 64, 2, 0, 0.125, None) == codes["FA_ERR_SHAPE"]
-    assert f32(p, p, p, p, p, 512, 32, 1, 0, 0.125, None) == codes["FA_ERR_HEAD_DIM"]
+    assert f32(p, p, p, p, p, 512, 20, 1, 0, 0.125, None) == codes["FA_ERR_HEAD_DIM"]
     assert f32(p, p, p, p, odd, 512, 64, 1, 0, 0.125, None) == codes["FA_ERR_ALIGN"]
     assert lib.fa_gemm_act(p, p, p, 128, 100, 64, 64, 100, 100, 0, None) == codes["FA_ERR_SHAPE"]
     assert lib.fa_gemm_act(p, p, p, 128, 128, 64, 64, 128, 128, 7, None) == codes["FA_ERR_ARG"]
     assert lib.fa_gemm_act(p, p, p, 128, 128, 64, 60, 128, 128, 0, None) == \
         codes["FA_ERR_STRIDE"]
+    assert lib.fa_gemm_act_f16(p, p, p, 128, 100, 64, 64, 100, 100, 0, None) == \
+        codes["FA_ERR_SHAPE"]
+    assert lib.fa_mlp_fwd_f16(p, p, p, None, p, 128, 64, 256, 2, None) == codes["FA_ERR_NULL"]
     assert lib.fa_selftest_wait_timeout(0, None) == codes["FA_ERR_ARG"]
     fn = lib.fa_mlp_fwd_noalloc
     assert fn(p, p, p, p, 4096, 64, 4096, 2, None) == codes["FA_ERR_SCRATCH"]

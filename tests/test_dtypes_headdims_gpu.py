@@ -1,0 +1,157 @@
+"""fp16 operands, head dims other than 64 / 128, and fp32 batched inputs,
+through the C ABI, against the CPU oracle.
+
+The reference's harnesses default to fp16 (bench.py:32 DTYPE_MAP,
+old/benchmark.py:96 --dtype fp16), its search takes any head dim
+(run_attention_search.py:187 --d) and its seeded runs are fp32
+(run_attention_search.py:169-181).  Tolerance as everywhere: max abs <= 2e-2,
+mean abs <= 2e-3 against the fp32 oracle on the same (rounded) inputs.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_close
+import oracle
+from cs348k_fast_attention_grammar_b200 import (attention, attention_bshd, attention_f32,
+                                                device_status, gemm_act, mlp)
+from cs348k_fast_attention_grammar_b200 import kernel_module
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _rand(shape, seed, dtype, amp=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * amp).to(dtype)
+
+
+def _oracle(q, k, v, causal):
+    return oracle.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                            causal=causal)
+
+
+@pytest.mark.parametrize("D", [64, 128, 96, 40])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("B,H,S", [(1, 2, 384), (2, 1, 200), (1, 1, 1000)])
+def test_fp16_attention_matches_oracle(B, H, S, D, causal):
+    q, k, v = (_rand((B, H, S, D), 300 + i, torch.float16) for i in range(3))
+    o = attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    torch.cuda.synchronize()
+    assert o.dtype == torch.float16
+    assert_close(o.float().cpu().numpy(), _oracle(q, k, v, causal),
+                 what=f"fp16 B{B} H{H} S{S} D{D} causal={causal}")
+
+
+def test_fp16_is_computed_in_fp16_not_bf16():
+    """Inputs whose low mantissa bits matter: fp16 keeps 10 bits, bf16 would
+    keep 7, so an fp16 run must match the oracle on the fp16 values far more
+    closely than the same values rounded to bf16 do."""
+    B, H, S, D = 1, 2, 256, 64
+    q, k, v = (_rand((B, H, S, D), 310 + i, torch.float16, amp=0.5) for i in range(3))
+    o = attention(q.to(DEV), k.to(DEV), v.to(DEV)).float().cpu().numpy()
+    ref = _oracle(q, k, v, False)
+    ref_bf = _oracle(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), False)
+    err = np.abs(o - ref).mean()
+    assert err < 0.5 * np.abs(ref_bf - ref).mean(), err
+
+
+@pytest.mark.parametrize("D", [8, 16, 24, 32, 48, 56, 72, 80, 104, 112, 120])
+@pytest.mark.parametrize("causal", [False, True])
+def test_other_head_dims_bf16(D, causal):
+    B, H, S = 2, 2, 333
+    q, k, v = (_rand((B, H, S, D), 320 + i, torch.bfloat16) for i in range(3))
+    o = attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    torch.cuda.synchronize()
+    assert_close(o.float().cpu().numpy(), _oracle(q, k, v, causal),
+                 what=f"bf16 D{D} causal={causal}")
+
+
+@pytest.mark.parametrize("D", [32, 96])
+def test_other_head_dims_strided_and_padded_output(D):
+    """(B, S, H, D) layout as strides, and an output view with a wider row:
+    the padding columns of the kernel's tile must not be written."""
+    B, S, H = 2, 300, 3
+    q, k, v = (_rand((B, S, H, D), 330 + i, torch.float16).to(DEV) for i in range(3))
+    o = attention_bshd(q, k, v, causal=True)
+    ref = _oracle(q.permute(0, 2, 1, 3).cpu(), k.permute(0, 2, 1, 3).cpu(),
+                  v.permute(0, 2, 1, 3).cpu(), True)
+    assert_close(o.permute(0, 2, 1, 3).float().cpu().numpy(), ref, what=f"bshd fp16 D{D}")
+    wide = torch.full((B, H, S, D + 8), 7.0, dtype=torch.float16, device=DEV)
+    attention(q.permute(0, 2, 1, 3), k.permute(0, 2, 1, 3), v.permute(0, 2, 1, 3),
+              causal=True, out=wide[..., :D])
+    torch.cuda.synchronize()
+    assert torch.all(wide[..., D:] == 7.0)
+    assert_close(wide[..., :D].float().cpu().numpy(), ref, what=f"padded out D{D}")
+
+
+@pytest.mark.parametrize("D", [64, 128, 48])
+@pytest.mark.parametrize("causal", [False, True])
+def test_fp32_batched_matches_oracle_and_2d_entry(D, causal):
+    B, H, S = 2, 3, 200
+    q, k, v = (_rand((B, H, S, D), 340 + i, torch.float32) for i in range(3))
+    o = attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    torch.cuda.synchronize()
+    assert o.dtype == torch.float32
+    rb = lambda t: t.to(torch.bfloat16)  # noqa: E731
+    assert_close(o.cpu().numpy(), _oracle(rb(q), rb(k), rb(v), causal),
+                 what=f"fp32 batched D{D} causal={causal}")
+    o2 = attention_f32(q[1, 2].to(DEV), k[1, 2].to(DEV), v[1, 2].to(DEV), causal=causal)
+    assert torch.equal(o2, o[1, 2])
+
+
+def test_kernel_module_fp16_arrays():
+    N, D = 512, 64
+    KT = _rand((D, N), 350, torch.float16)
+    Q = _rand((N, D), 351, torch.float16)
+    V = _rand((N, D), 352, torch.float16)
+    out = kernel_module.fn(KT.to(DEV), Q.to(DEV), V.to(DEV))
+    assert out.dtype == torch.float16 and tuple(out.shape) == (N, D)
+    ref = oracle.naive_fn(KT.float().numpy(), Q.float().numpy(), V.float().numpy())
+    assert_close(out.float().cpu().numpy(), ref, what="kernel_module.fn fp16")
+
+
+def test_legacy_benchmark_shape_fp16_subset():
+    """old/benchmark.py:90-93's shape (B8 S2048 H16 D64, fp16, (B, S, H, D)):
+    every head of two batch rows against the oracle."""
+    B, S, H, D = 8, 2048, 16, 64
+    q, k, v = (_rand((B, S, H, D), 360 + i, torch.float16).to(DEV) for i in range(3))
+    o = attention_bshd(q, k, v)
+    torch.cuda.synchronize()
+    for b in (0, 5):
+        ref = _oracle(q[b:b + 1].permute(0, 2, 1, 3).cpu(), k[b:b + 1].permute(0, 2, 1, 3).cpu(),
+                      v[b:b + 1].permute(0, 2, 1, 3).cpu(), False)
+        assert_close(o[b:b + 1].permute(0, 2, 1, 3).float().cpu().numpy(), ref,
+                     what=f"legacy fp16 batch {b}")
+    assert device_status() == 0
+
+
+@pytest.mark.parametrize("M,K,N", [(512, 256, 1024), (2048, 512, 2048), (130, 192, 320)])
+@pytest.mark.parametrize("act", ["gelu_tanh", "relu"])
+def test_fp16_mlp_matches_oracle(M, K, N, act):
+    """fp16 MLP block (one-SM and two-SM GEMM tiles, ragged M) against the
+    oracle, with the hidden activation rounded to fp16 as the kernel stores it."""
+    x = _rand((M, K), 370, torch.float16)
+    w1 = _rand((K, N), 371, torch.float16, amp=K ** -0.5)
+    w2 = _rand((N, K), 372, torch.float16, amp=N ** -0.5)
+    y = mlp(x.to(DEV), w1.to(DEV), w2.to(DEV), act=act)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float16
+    h = oracle.mlp(x.float().numpy(), w1.float().numpy(), np.eye(N), act=act)
+    h16 = torch.from_numpy(h.astype(np.float32)).to(torch.float16).double().numpy()
+    ref = h16 @ w2.double().numpy()
+    assert_close(y.float().cpu().numpy(), ref, what=f"fp16 mlp M{M} K{K} N{N} {act}")
+
+
+def test_fp16_gemm_and_dtype_errors():
+    a = _rand((256, 128), 380, torch.float16).to(DEV)
+    b = _rand((128, 192), 381, torch.float16, amp=128 ** -0.5).to(DEV)
+    c = gemm_act(a, b, act="none")
+    ref = a.double().cpu().numpy() @ b.double().cpu().numpy()
+    assert c.dtype == torch.float16
+    assert_close(c.float().cpu().numpy(), ref, what="fp16 gemm")
+    with pytest.raises(TypeError):
+        gemm_act(a, b.to(torch.bfloat16))
+    with pytest.raises(TypeError):
+        mlp(a, b.to(torch.bfloat16), b.t().contiguous())
