@@ -14,6 +14,8 @@ import threading
 from . import build as _build
 
 FA_OK = 0
+FA_F32_BF16 = 0
+FA_F32_SPLIT = 1
 FA_ACT_NONE = 0
 FA_ACT_RELU = 1
 FA_ACT_GELU_TANH = 2
@@ -31,7 +33,7 @@ SIGNATURES = {
     "fa_attn_fwd_f32": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
                                  _c_float, _vp]),
     "fa_attn_fwd_f32_batched": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
-                                         _c_int, _c_int, _c_float, _vp]),
+                                         _c_int, _c_int, _c_int, _c_float, _c_int, _vp]),
     "fa_gemm_act": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _i64, _i64, _i64,
                              _c_int, _vp]),
     "fa_gemm_act_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _i64, _i64, _i64,

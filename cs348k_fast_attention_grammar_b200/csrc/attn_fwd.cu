@@ -314,13 +314,22 @@ __device__ __forceinline__ void decode_unit(const AttnParams& p, int unit, int& 
   }
 }
 
-template <int D, bool CAUSAL, bool OUT_F32, bool F16>
+// SPLIT (fp32 inputs at head dim <= 64, D = 128 here): every operand row is
+// [hi | lo] -- the bf16 rounding of the fp32 value in the first 64 columns and
+// the bf16 rounding of its remainder in the next 64 -- and the kernel forms
+// S = Qh Kh^T + Qh Kl^T + Ql Kh^T and O = Ph Vh + Ph Vl + Pl Vh (the lo*lo
+// terms are below fp32 rounding of the result), all accumulated in fp32, so
+// the inputs keep about 16 significant bits instead of bf16's 8.  Ph / Pl are
+// written to columns [0, 64) / [64, 128) of S_t; O uses 64 of its columns.
+template <int D, bool CAUSAL, bool OUT_F32, bool F16, bool SPLIT = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using C = AttnCfg<D>;
-  constexpr int kEmuMod = (D == 64) ? FA_ATTN_EMU_MOD_D64 : FA_ATTN_EMU_MOD_D128;
+  // The split mode keeps every exponential on MUFU (ex2.approx, relative
+  // error ~2^-22): the FMA-pipe polynomial's 7.5e-5 would dominate its error.
+  constexpr int kEmuMod = SPLIT ? 0 : (D == 64) ? FA_ATTN_EMU_MOD_D64 : FA_ATTN_EMU_MOD_D128;
   constexpr bool kPackAlu = FA_ATTN_PACK_ALU != 0 && !F16;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -468,8 +477,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 9) {
     // =================== MMA issuer ===================
     if (elect_one()) {
+      static_assert(!SPLIT || (D == 128 && !F16), "the split mode is bf16 hi/lo at D = 128");
       constexpr uint32_t kIdQK = idesc_f32acc(kBM, kBN, false, false, F16);
-      constexpr uint32_t kIdPV = idesc_f32acc(kBM, D, false, true, F16);
+      constexpr uint32_t kIdPV = idesc_f32acc(kBM, SPLIT ? 64 : D, false, true, F16);
       bool ok = true;
       int it = 0;              // K/V tiles consumed, over all units (ring position)
       int pb[2] = {0, 0};      // key blocks of tile t in earlier units (P phases)
@@ -519,8 +529,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int kk = kk0; kk < kk1; ++kk) {
                 const uint64_t bdesc = sdesc_sw128(vbase + kk * 2048, 16384, 1024);
-                mma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8, bdesc, kIdPV,
-                       (j - 1 > 0 || kk > 0) ? 1u : 0u);
+                const uint32_t acc = (j - 1 > 0 || kk > 0) ? 1u : 0u;
+                if (SPLIT) {
+                  // Ph Vh + Ph Vl + Pl Vh: Vl is the second 64-column atom of
+                  // the V tile, Pl sits 64 columns after Ph.
+                  const uint64_t vl = sdesc_sw128(vbase + 16384 + kk * 2048, 16384, 1024);
+                  const uint32_t ph = tmem + C::col_s(t) + kk * 8;
+                  mma_ts(tmem + C::col_o(t), ph, bdesc, kIdPV, acc);
+                  mma_ts(tmem + C::col_o(t), ph, vl, kIdPV, 1u);
+                  mma_ts(tmem + C::col_o(t), ph + 64, bdesc, kIdPV, 1u);
+                } else {
+                  mma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8, bdesc, kIdPV, acc);
+                }
               }
             }
             if (!ok) break;
@@ -530,11 +550,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             // S_t = Q_t K_j^T: both K-major, 64-element swizzle atoms 16 KiB apart.
             const uint32_t qbase = sQ + t * C::kTileBytes;
             const uint32_t kbase = sKV + kslot * C::kTileBytes;
+            if (SPLIT) {
+              // Qh Kh^T + Qh Kl^T + Ql Kh^T over the 64 logical columns: hi
+              // atoms at +0, lo atoms at +16 KiB.
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-              mma_ss(tmem + C::col_s(t), sdesc_sw128(qbase + off, 16, 1024),
-                     sdesc_sw128(kbase + off, 16, 1024), kIdQK, kk > 0 ? 1u : 0u);
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t qh = sdesc_sw128(qbase + kk * 32, 16, 1024);
+                const uint64_t kh = sdesc_sw128(kbase + kk * 32, 16, 1024);
+                mma_ss(tmem + C::col_s(t), qh, kh, kIdQK, kk > 0 ? 1u : 0u);
+                mma_ss(tmem + C::col_s(t), qh, sdesc_sw128(kbase + 16384 + kk * 32, 16, 1024),
+                       kIdQK, 1u);
+                mma_ss(tmem + C::col_s(t), sdesc_sw128(qbase + 16384 + kk * 32, 16, 1024), kh,
+                       kIdQK, 1u);
+              }
+            } else {
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                mma_ss(tmem + C::col_s(t), sdesc_sw128(qbase + off, 16, 1024),
+                       sdesc_sw128(kbase + off, 16, 1024), kIdQK, kk > 0 ? 1u : 0u);
+              }
             }
             mma_commit(bar_s_full(t));
             FA_TRACE(j, 13 + 2 * t);
@@ -667,6 +702,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t sl2x2 = f2_pack(sl2, sl2);
       const uint64_t negm2 = f2_pack(neg_m, neg_m);
       uint32_t pk[2][32];
+      uint32_t pl[2][32];    // SPLIT: bf16 remainders of the probabilities
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
 #pragma unroll
@@ -696,10 +732,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           else
             rs[c & 3] += p0 + p1;
           pk[half][cc] = kPackAlu ? pack_bf16x2_alu(p0, p1) : pack_16x2<F16>(p0, p1);
+          if (SPLIT)
+            pl[half][cc] = pack_bf16x2(p0 - __uint_as_float(pk[half][cc] << 16),
+                                       p1 - __uint_as_float(pk[half][cc] & 0xffff0000u));
         }
         if (FA_ATTN_SPLIT_P && half == 0) {
           // keys 0-63 of P -> TMEM columns [0, 32); the MMA warp starts on them
           tmem_st32(tS, pk[0]);
+          if (SPLIT) tmem_st32(tS + 64, pl[0]);
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(bar_p_half(t));
@@ -715,7 +755,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       }
       if (!FA_ATTN_SPLIT_P) tmem_st32(tS, pk[0]);
+      if (!FA_ATTN_SPLIT_P && SPLIT) tmem_st32(tS + 64, pl[0]);
       tmem_st32(tS + 32, pk[1]);
+      if (SPLIT) tmem_st32(tS + 96, pl[1]);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_p_full(t));
@@ -782,11 +824,11 @@ int launch_maybe_pdl(Kern kern, int grid, int threads, int smem, cudaStream_t st
   return cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, prm) == cudaSuccess ? FA_OK : FA_ERR_LAUNCH;
 }
 
-template <int D, bool CAUSAL, bool OUT_F32, bool F16>
+template <int D, bool CAUSAL, bool OUT_F32, bool F16, bool SPLIT = false>
 int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                 const AttnParams& prm, int grid, cudaStream_t stream, bool pdl) {
   using C = AttnCfg<D>;
-  auto kern = attn_fwd_kernel<D, CAUSAL, OUT_F32, F16>;
+  auto kern = attn_fwd_kernel<D, CAUSAL, OUT_F32, F16, SPLIT>;
   static KernelPrep prep;
   int dev = 0;
   const int rc = prepare_kernel(prep, reinterpret_cast<const void*>(kern), C::kSmemBytes, &dev);
@@ -1290,15 +1332,17 @@ namespace {
 
 // Shared host path of fa_attn_fwd / fa_attn_fwd_f32 (arguments already
 // validated): tensor maps, scheduling groups, launch.
+// d_out: head dim of O when it differs from the operands' D (split mode:
+// operand rows of 128 [hi | lo] values for a head dim <= 64).
 int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H, int S, int D,
              const int64_t* st, int causal, float scale, bool out_f32, bool f16,
-             cudaStream_t stream, bool pdl = false) {
+             cudaStream_t stream, bool pdl = false, bool split = false, int d_out = 0) {
   int dev = 0;
   int rc = prepare_device(nullptr, 0, &dev);
   if (rc != FA_OK) return rc;
   // D <= 64: four-tile kernel with 64-key blocks; D <= 128: two-tile kernel.
   // Head dims below the kernel's width are zero-padded by the tensor maps.
-  const bool q4 = (D <= 64);
+  const bool q4 = (D <= 64) && !split;
   const int kv_rows = q4 ? kQ4BN : kBN;                  // keys per K/V block
   // Tiles per work unit: the kernel's width, halved while at most half the
   // SMs would get a unit (small problems spread over more SMs; a unit's
@@ -1320,7 +1364,7 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
   prm.B = B;
   prm.H = H;
   prm.S = S;
-  prm.D = D;
+  prm.D = d_out > 0 ? d_out : D;
   prm.n_units_per_head = (S + unit_rows - 1) / unit_rows;
   // Groups: at most FA_ATTN_GROUP_MIB of K/V each (>= 1 pair), the pairs
   // split as evenly as possible over them, since a short last group starts its
@@ -1363,6 +1407,10 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
     return causal ? launch_attn_q4<true, false, false>(mq, mk, mv, prm, grid, stream, pdl)
                   : launch_attn_q4<false, false, false>(mq, mk, mv, prm, grid, stream, pdl);
   }
+  if (split)
+    return causal ? launch_attn<128, true, true, false, true>(mq, mk, mv, prm, grid, stream, pdl)
+                  : launch_attn<128, false, true, false, true>(mq, mk, mv, prm, grid, stream,
+                                                               pdl);
   if (out_f32)
     return causal ? launch_attn<128, true, true, false>(mq, mk, mv, prm, grid, stream, pdl)
                   : launch_attn<128, false, true, false>(mq, mk, mv, prm, grid, stream, pdl);
@@ -1373,47 +1421,58 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
                 : launch_attn<128, false, false, false>(mq, mk, mv, prm, grid, stream, pdl);
 }
 
-// fp32 -> bf16 staging of the reference's 2-D operands into the workspace
-// [q | k | v], each [N, D] row-major.  blockIdx.z picks the tensor; K comes
-// either as [N, D] or transposed as KT [D, N] (then a 32 x 32 tile goes
-// through shared memory so reads and writes both stay coalesced).
+// fp32 -> bf16 staging of q, k, v (blockIdx.z picks the tensor) into the
+// workspace [q | k | v].  Rows are the flattened (batch, head, position)
+// index, S positions per (batch, head) matrix; K comes as [.., S, D] or, with
+// k_transposed, as KT [.., D, S] (a 32 x 32 tile then goes through shared
+// memory so reads and writes both stay coalesced).  split = 0: workspace
+// rows of D bf16 values.  split = 1: rows of 128 values [hi | lo]: hi =
+// bf16(x) in columns [0, D), lo = bf16(x - hi) in [64, 64 + D), zeros in the
+// padding columns (the split-mode attention reads both 64-column atoms).
 __global__ void __launch_bounds__(256)
     stage_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
-                     const float* __restrict__ v, __nv_bfloat16* __restrict__ ws, int64_t N,
-                     int D, int k_transposed) {
+                     const float* __restrict__ v, __nv_bfloat16* __restrict__ ws, int64_t rows,
+                     int S, int D, int k_transposed, int split) {
   __shared__ float tile[32][33];
   // The attention kernel may start its set-up now; its loads wait for this
   // grid to complete.
   grid_dependents_launch();
   const int z = blockIdx.z;
   const float* src = (z == 0) ? q : (z == 1) ? k : v;
-  __nv_bfloat16* dst = ws + static_cast<int64_t>(z) * N * D;
+  const int W = split ? 128 : D;                       // workspace row width
+  __nv_bfloat16* dst = ws + static_cast<int64_t>(z) * rows * W;
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 32;
   const int d0 = blockIdx.y * 32;
   const int tx = threadIdx.x & 31;
   const int ty = threadIdx.x >> 5;   // 0..7
+  // Value of element (row, d); zero outside the tensor.
+  auto load = [&](int64_t row, int d) -> float {
+    if (row >= rows || d >= D) return 0.f;
+    if (z == 1 && k_transposed) {
+      const int64_t bh = row / S, n = row - bh * S;
+      return src[(bh * D + d) * S + n];
+    }
+    return src[row * D + d];
+  };
+  auto store = [&](int64_t row, int d, float x) {
+    if (row >= rows) return;
+    if (split) {
+      const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+      dst[row * 128 + d] = hi;
+      dst[row * 128 + 64 + d] = __float2bfloat16_rn(x - __bfloat162float(hi));
+    } else if (d < D) {
+      dst[row * D + d] = __float2bfloat16_rn(x);
+    }
+  };
   if (z == 1 && k_transposed) {
 #pragma unroll
-    for (int r = ty; r < 32; r += 8) {      // r = d within the tile, read along n
-      const int d = d0 + r, n = n0 + tx;
-      tile[r][tx] = (n < N && d < D) ? src[static_cast<int64_t>(d) * N + n] : 0.f;
-    }
+    for (int r = ty; r < 32; r += 8) tile[r][tx] = load(n0 + tx, d0 + r);   // read along n
     __syncthreads();
 #pragma unroll
-    for (int r = ty; r < 32; r += 8) {      // r = n within the tile, write along d
-      const int n = n0 + r;
-      if (n < N && d0 + tx < D)
-        dst[static_cast<int64_t>(n) * D + d0 + tx] = __float2bfloat16_rn(tile[tx][r]);
-    }
+    for (int r = ty; r < 32; r += 8) store(n0 + r, d0 + tx, tile[tx][r]);   // write along d
   } else {
 #pragma unroll
-    for (int r = ty; r < 32; r += 8) {
-      const int64_t n = static_cast<int64_t>(n0) + r;
-      if (n < N && d0 + tx < D) {
-        const int64_t i = n * D + d0 + tx;
-        dst[i] = __float2bfloat16_rn(src[i]);
-      }
-    }
+    for (int r = ty; r < 32; r += 8) store(n0 + r, d0 + tx, load(n0 + r, d0 + tx));
   }
 }
 
@@ -1478,24 +1537,30 @@ int check_attn_args(const void* q, const void* k, const void* v, const void* o, 
   return FA_OK;
 }
 
-// fp32 -> bf16 staging of n_rows rows of D values per tensor into ws, then the
-// attention with an fp32 epilogue, launched as a programmatic dependent.
+// fp32 -> bf16 staging of the B * H * S rows of each tensor into ws (split:
+// [hi | lo] rows of 128 values), then the attention with an fp32 epilogue,
+// launched as a programmatic dependent of the staging kernel.
 int run_attn_f32(const void* q, const void* k, const void* v, void* o, void* ws, int B, int H,
-                 int S, int D, int k_transposed, int causal, float scale, cudaStream_t s) {
+                 int S, int D, int k_transposed, int causal, float scale, bool split,
+                 cudaStream_t s) {
   int dev = 0;
   int rc = prepare_device(nullptr, 0, &dev);
   if (rc != FA_OK) return rc;
   __nv_bfloat16* wb = static_cast<__nv_bfloat16*>(ws);
   const int64_t rows = static_cast<int64_t>(B) * H * S;
-  const dim3 grid(static_cast<unsigned>((rows + 31) / 32), (D + 31) / 32, 3);
+  const int W = split ? 128 : D;
+  const dim3 grid(static_cast<unsigned>((rows + 31) / 32), split ? 2 : (D + 31) / 32, 3);
   stage_f32_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(q),
                                        static_cast<const float*>(k),
-                                       static_cast<const float*>(v), wb, rows, D, k_transposed);
+                                       static_cast<const float*>(v), wb, rows, S, D, k_transposed,
+                                       split ? 1 : 0);
   if (cudaGetLastError() != cudaSuccess) return FA_ERR_LAUNCH;
-  const int64_t sd = static_cast<int64_t>(S) * D, hsd = sd * H, n = hsd * B;
-  const int64_t st[16] = {hsd, sd, D, 1, hsd, sd, D, 1, hsd, sd, D, 1, hsd, sd, D, 1};
-  return run_attn(wb, wb + n, wb + 2 * n, o, B, H, S, D, st, causal, scale, true, false, s,
-                  /*pdl=*/true);
+  const int64_t n = rows * W;
+  const int64_t sw = static_cast<int64_t>(S) * W, hsw = sw * H;
+  const int64_t so = static_cast<int64_t>(S) * D, hso = so * H;   // O: fp32 [B, H, S, D]
+  const int64_t st[16] = {hsw, sw, W, 1, hsw, sw, W, 1, hsw, sw, W, 1, hso, so, D, 1};
+  return run_attn(wb, wb + n, wb + 2 * n, o, B, H, S, W, st, causal, scale, true, false, s,
+                  /*pdl=*/true, split, D);
 }
 
 }  // namespace
@@ -1532,24 +1597,25 @@ extern "C" int fa_attn_fwd_f32(const void* q, const void* k, const void* v, void
   const void* ptrs[5] = {q, k, v, o, ws};
   for (int t = 0; t < 5; ++t)
     if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 != 0) return FA_ERR_ALIGN;
-  return run_attn_f32(q, k, v, o, ws, 1, 1, N, D, k_transposed, causal, scale,
+  return run_attn_f32(q, k, v, o, ws, 1, 1, N, D, k_transposed, causal, scale, false,
                       static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int fa_attn_fwd_f32_batched(const void* q, const void* k, const void* v, void* o,
-                                       void* ws, int B, int H, int S, int D, int causal,
-                                       float scale, void* stream) {
+                                       void* ws, int B, int H, int S, int D, int k_transposed,
+                                       int causal, float scale, int precision, void* stream) {
   using namespace fa;
   if (!q || !k || !v || !o || !ws) return FA_ERR_NULL;
-  if (B <= 0 || H <= 0 || S <= 0) return FA_ERR_SHAPE;
-  if (!head_dim_ok(D)) return FA_ERR_HEAD_DIM;
+  if (B <= 0 || H <= 0 || S <= 0 || (k_transposed != 0 && k_transposed != 1)) return FA_ERR_SHAPE;
+  if (precision != FA_F32_BF16 && precision != FA_F32_SPLIT) return FA_ERR_ARG;
+  if (!head_dim_ok(D) || (precision == FA_F32_SPLIT && D > 64)) return FA_ERR_HEAD_DIM;
   const int64_t rows = static_cast<int64_t>(B) * H * S;
-  if (rows * D > (1ll << 34) || (rows + 31) / 32 > 0x7fffffffLL ||
+  if (rows * 128 > (1ll << 34) || (rows + 31) / 32 > 0x7fffffffLL ||
       static_cast<int64_t>(B) * H * ((S + kBM - 1) / kBM) > 0x7fffffffLL)
     return FA_ERR_SHAPE;
   const void* ptrs[5] = {q, k, v, o, ws};
   for (int t = 0; t < 5; ++t)
     if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 != 0) return FA_ERR_ALIGN;
-  return run_attn_f32(q, k, v, o, ws, B, H, S, D, 0, causal, scale,
-                      static_cast<cudaStream_t>(stream));
+  return run_attn_f32(q, k, v, o, ws, B, H, S, D, k_transposed, causal, scale,
+                      precision == FA_F32_SPLIT, static_cast<cudaStream_t>(stream));
 }

@@ -8,9 +8,10 @@ order (``grammar/kernel_ast.py:673``) and ``KERNEL_META`` (``:1280-1287``).
 The reference's arrays are DLPack-capable (cupy); they are wrapped with
 ``torch.from_dlpack`` as ``pytorch-naive.py:36-38`` does.  fp16 and bf16
 arrays run the tensor cores in their own type (fp32 accumulate); fp32 arrays
-(the reference's default) are staged to bf16 on the device in the same C
-call, with an fp32 result.  As in the reference, the callee allocates and
-returns the output.
+(the reference's default) are staged on the device in the same C call as
+bf16 hi + lo pairs whose three significant products the GEMMs accumulate
+(about 16 significant bits), with an fp32 result.  As in the reference, the
+callee allocates and returns the output.
 """
 
 from __future__ import annotations
@@ -46,11 +47,13 @@ def _as_torch(x) -> torch.Tensor:
 def fn(KT, Q, V):
     """``fn(KT, Q, V) -> O`` for ``KT [d, N]``, ``Q [N, d]``, ``V [N, d]``
     (the signature of ``pytorch-naive.py:23`` and every emitted module).
-    fp32 inputs go through one C call (device-side bf16 staging, fp32 output);
-    bf16 and fp16 inputs through the batched operator, in their own type."""
+    fp32 inputs go through one C call (device-side hi/lo staging, fp32
+    output; head dims above 64 fall back to plain bf16 staging); bf16 and fp16
+    inputs through the batched operator, in their own type."""
     KT, Q, V = _as_torch(KT), _as_torch(Q), _as_torch(V)
     if Q.dtype == torch.float32:
-        return attention_f32(Q.contiguous(), KT.contiguous(), V.contiguous(), k_transposed=True)
+        return attention_f32(Q.contiguous(), KT.contiguous(), V.contiguous(), k_transposed=True,
+                             precise=Q.shape[1] <= 64)
     # bf16 / fp16: K must be contiguous along d, so KT [d, N] is transposed once.
     q = Q.contiguous().unsqueeze(0).unsqueeze(0)
     k = KT.t().contiguous().unsqueeze(0).unsqueeze(0)
@@ -62,4 +65,6 @@ def sota_fn(K, Q, V):
     """``fn(K, Q, V)`` on ``[B, H, S, D]`` tensors, the argument order of
     ``flash-attn2-sota.py:41``."""
     K, Q, V = _as_torch(K), _as_torch(Q), _as_torch(V)
-    return attention(Q.contiguous(), K.contiguous(), V.contiguous(), causal=False)
+    precise = Q.dtype == torch.float32 and Q.shape[-1] <= 64
+    return attention(Q.contiguous(), K.contiguous(), V.contiguous(), causal=False,
+                     precise=precise)

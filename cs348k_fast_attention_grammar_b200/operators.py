@@ -111,7 +111,8 @@ def _check_cuda_bf16(name: str, t: torch.Tensor) -> None:
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
-              scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+              scale: float | None = None, out: torch.Tensor | None = None,
+              precise: bool = False) -> torch.Tensor:
     """softmax(q k^T * scale [+ causal mask]) v on ``[B, H, S, D]`` CUDA tensors.
 
     ``scale`` defaults to ``1/sqrt(D)`` (``run_attention_search.py:40``); D is
@@ -120,7 +121,10 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
     have arbitrary batch/head/sequence strides (multiples of 8 elements) but
     must be contiguous along D.  fp32 inputs (the reference's dtype) must be
     contiguous; they are staged to bf16 on the device in the same C call and
-    O is written in fp32.  Returns a new ``[B, H, S, D]`` tensor of the input
+    O is written in fp32.  With ``precise`` (fp32 inputs, D <= 64) every
+    operand is staged as a bf16 hi + lo pair and the GEMMs take the three
+    significant products (about 16 significant bits instead of 8, three times
+    the tensor-core work).  Returns a new ``[B, H, S, D]`` tensor of the input
     dtype unless ``out`` is given.
     """
     for name, t in (("q", q), ("k", k), ("v", v)):
@@ -151,14 +155,18 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
         for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
             if not t.is_contiguous():
                 raise ValueError(f"fp32 {name} must be contiguous")
+        mode = _lib.FA_F32_SPLIT if precise else _lib.FA_F32_BF16
+        width = 128 if precise else D
         with _on_device(q.device):
             stream = _stream_ptr(q.device)
-            ws = _staging_workspace(3 * q.numel(), q.device, stream)
+            ws = _staging_workspace(3 * B * H * S * width, q.device, stream)
             rc = lib.fa_attn_fwd_f32_batched(q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                             out.data_ptr(), ws.data_ptr(), B, H, S, D,
-                                             int(bool(causal)), float(scale), stream)
+                                             out.data_ptr(), ws.data_ptr(), B, H, S, D, 0,
+                                             int(bool(causal)), float(scale), mode, stream)
         _lib.check(rc, "fa_attn_fwd_f32_batched")
         return out
+    if precise:
+        raise ValueError("precise applies to fp32 inputs")
     strides = (ctypes.c_int64 * 16)(*q.stride(), *k.stride(), *v.stride(), *out.stride())
     fn, where = ((lib.fa_attn_fwd_f16, "fa_attn_fwd_f16") if dtype == _F16
                  else (lib.fa_attn_fwd, "fa_attn_fwd"))
@@ -171,12 +179,13 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
 
 def attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
                   scale: float | None = None, k_transposed: bool = False,
-                  out: torch.Tensor | None = None) -> torch.Tensor:
+                  out: torch.Tensor | None = None, precise: bool = False) -> torch.Tensor:
     """The reference's own 2-D fp32 problem: ``q [N, D]``, ``k [N, D]`` (or
     ``KT [D, N]`` with ``k_transposed=True``), ``v [N, D]`` contiguous fp32
     CUDA tensors -> ``o [N, D]`` fp32.  One C call: the operands are staged to
     bf16 on the device and the attention epilogue writes fp32 (the
-    ``fn(KT, Q, V)`` of ``pytorch-naive.py:23`` and the emitted modules)."""
+    ``fn(KT, Q, V)`` of ``pytorch-naive.py:23`` and the emitted modules).
+    ``precise`` stages bf16 hi + lo pairs instead (D <= 64), see ``attention``."""
     for name, t in (("q", q), ("k", k), ("v", v)):
         if not isinstance(t, torch.Tensor):
             raise TypeError(f"{name} must be a torch.Tensor")
@@ -200,11 +209,20 @@ def attention_f32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
     lib = _lib.load()
     with _on_device(q.device):
         stream = _stream_ptr(q.device)
-        ws = _staging_workspace(3 * N * D, q.device, stream)
-        rc = lib.fa_attn_fwd_f32(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-                                 ws.data_ptr(), N, D, int(bool(k_transposed)),
-                                 int(bool(causal)), float(scale), stream)
-    _lib.check(rc, "fa_attn_fwd_f32")
+        if precise:
+            ws = _staging_workspace(3 * N * 128, q.device, stream)
+            rc = lib.fa_attn_fwd_f32_batched(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                             out.data_ptr(), ws.data_ptr(), 1, 1, N, D,
+                                             int(bool(k_transposed)), int(bool(causal)),
+                                             float(scale), _lib.FA_F32_SPLIT, stream)
+            where = "fa_attn_fwd_f32_batched"
+        else:
+            ws = _staging_workspace(3 * N * D, q.device, stream)
+            rc = lib.fa_attn_fwd_f32(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                     ws.data_ptr(), N, D, int(bool(k_transposed)),
+                                     int(bool(causal)), float(scale), stream)
+            where = "fa_attn_fwd_f32"
+    _lib.check(rc, where)
     return out
 
 

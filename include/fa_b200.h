@@ -60,6 +60,11 @@ typedef enum fa_status {
   FA_ERR_SCRATCH = 13      /* problem exceeds fa_mlp_fwd_noalloc's fixed buffer */
 } fa_status;
 
+typedef enum fa_f32_precision {
+  FA_F32_BF16 = 0,         /* fp32 operands rounded to bf16 (8 significant bits) */
+  FA_F32_SPLIT = 1         /* bf16 hi + lo split, three products per GEMM        */
+} fa_f32_precision;
+
 typedef enum fa_activation {
   FA_ACT_NONE = 0,
   FA_ACT_RELU = 1,         /* run_mlp_search.py:62-64                           */
@@ -121,12 +126,21 @@ int fa_attn_fwd_f32(const void* q, const void* k, const void* v, void* o, void* 
                     int D, int k_transposed, int causal, float scale, void* stream);
 
 /*
- * fa_attn_fwd_f32 for batched tensors: q, k, v, o contiguous [B, H, S, D]
- * fp32; ws a bf16 workspace of 3 * B * H * S * D elements (16-byte aligned).
- * Staging and attention as fa_attn_fwd_f32 (two launches for all pairs).
+ * fp32 attention for batched tensors: q, v, o contiguous [B, H, S, D] fp32,
+ * k contiguous [B, H, S, D] (k_transposed = 0) or [B, H, D, S] (1).  Two
+ * launches for all pairs: staging to bf16, then the attention with an fp32
+ * epilogue.  precision:
+ *   FA_F32_BF16  : operands rounded to bf16 (as fa_attn_fwd_f32);
+ *                  ws = 3 * B * H * S * D bf16 elements;
+ *   FA_F32_SPLIT : each operand x staged as hi = bf16(x) and lo = bf16(x - hi),
+ *                  and S = Qh Kh^T + Qh Kl^T + Ql Kh^T, O = Ph Vh + Ph Vl + Pl Vh
+ *                  accumulated in fp32 (about 16 significant bits; three times
+ *                  the tensor-core work); D <= 64; ws = 3 * B * H * S * 128.
+ * ws is 16-byte aligned.
  */
 int fa_attn_fwd_f32_batched(const void* q, const void* k, const void* v, void* o, void* ws,
-                            int B, int H, int S, int D, int causal, float scale, void* stream);
+                            int B, int H, int S, int D, int k_transposed, int causal,
+                            float scale, int precision, void* stream);
 
 /*
  * C[M, N] = act(A[M, K] @ B[K, N]) in bf16 with fp32 accumulation.

@@ -69,10 +69,13 @@ def test_argument_checks_without_device():
     assert lib.fa_attn_fwd_f16(None, p, p, p, 1, 1, 16, 64, st, 0, 0.125, None) == \
         codes["FA_ERR_NULL"]
     b32 = lib.fa_attn_fwd_f32_batched
-    assert b32(p, p, p, p, None, 1, 4, 256, 64, 0, 0.125, None) == codes["FA_ERR_NULL"]
-    assert b32(p, p, p, p, p, 1, 0, 256, 64, 0, 0.125, None) == codes["FA_ERR_SHAPE"]
-    assert b32(p, p, p, p, p, 1, 4, 256, 72 + 4, 0, 0.125, None) == codes["FA_ERR_HEAD_DIM"]
-    assert b32(p, p, p, odd, p, 1, 4, 256, 64, 0, 0.125, None) == codes["FA_ERR_ALIGN"]
+    assert b32(p, p, p, p, None, 1, 4, 256, 64, 0, 0, 0.125, 0, None) == codes["FA_ERR_NULL"]
+    assert b32(p, p, p, p, p, 1, 0, 256, 64, 0, 0, 0.125, 0, None) == codes["FA_ERR_SHAPE"]
+    assert b32(p, p, p, p, p, 1, 4, 256, 64, 2, 0, 0.125, 0, None) == codes["FA_ERR_SHAPE"]
+    assert b32(p, p, p, p, p, 1, 4, 256, 76, 0, 0, 0.125, 0, None) == codes["FA_ERR_HEAD_DIM"]
+    assert b32(p, p, p, p, p, 1, 4, 256, 72, 0, 0, 0.125, 1, None) == codes["FA_ERR_HEAD_DIM"]
+    assert b32(p, p, p, p, p, 1, 4, 256, 64, 0, 0, 0.125, 2, None) == codes["FA_ERR_ARG"]
+    assert b32(p, p, p, odd, p, 1, 4, 256, 64, 0, 0, 0.125, 0, None) == codes["FA_ERR_ALIGN"]
     bad = (ctypes.c_int64 * 16)(*([8192, 1024, 65, 1] * 4))
     assert lib.fa_attn_fwd(p, p, p, p, 1, 1, 16, 64, bad, 0, 0.125, None) == codes["FA_ERR_ALIGN"]
     bad = (ctypes.c_int64 * 16)(*([8192, 1024, 64, 2] * 4))

@@ -155,3 +155,41 @@ def test_fp16_gemm_and_dtype_errors():
         gemm_act(a, b.to(torch.bfloat16))
     with pytest.raises(TypeError):
         mlp(a, b.to(torch.bfloat16), b.t().contiguous())
+
+
+@pytest.mark.parametrize("D", [64, 32, 56])
+@pytest.mark.parametrize("causal", [False, True])
+def test_fp32_split_precision_against_fp32_inputs(D, causal):
+    """precise=True (bf16 hi + lo operands, three products per GEMM, fp32
+    accumulation) against the fp64 oracle on the fp32 inputs themselves --
+    no bf16 rounding of the inputs in the reference -- at a tolerance 100x
+    tighter than the bf16 bar, and at least 20x closer than the bf16 staging
+    of the same inputs."""
+    B, H, S = 1, 3, 333
+    q, k, v = (_rand((B, H, S, D), 390 + i, torch.float32) for i in range(3))
+    ref = _oracle(q, k, v, causal)
+    o = attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal, precise=True)
+    o_bf = attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    torch.cuda.synchronize()
+    assert_close(o.cpu().numpy(), ref, max_tol=2e-4, mean_tol=2e-5,
+                 what=f"split fp32 D{D} causal={causal}")
+    err = np.abs(o.cpu().numpy() - ref).mean()
+    err_bf = np.abs(o_bf.cpu().numpy() - ref).mean()
+    assert err * 20 < err_bf, (err, err_bf)
+
+
+def test_fp32_split_2d_entry_kt_layout_and_kernel_module():
+    """The reference's own problem (fn(KT, Q, V), N = 512, d = 64, fp32):
+    kernel_module.fn takes the split path, K given transposed."""
+    N, D = 512, 64
+    g = torch.Generator().manual_seed(400)
+    KT, Q, V = (torch.randn(s, generator=g) for s in ((D, N), (N, D), (N, D)))
+    out = kernel_module.fn(KT.to(DEV), Q.to(DEV), V.to(DEV))
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float32
+    ref = oracle.naive_fn(KT.double().numpy(), Q.double().numpy(), V.double().numpy())
+    assert_close(out.cpu().numpy(), ref, max_tol=2e-4, mean_tol=2e-5, what="kernel_module split")
+    o2 = attention_f32(Q.to(DEV), KT.to(DEV), V.to(DEV), k_transposed=True, precise=True)
+    assert torch.equal(o2, out)
+    with pytest.raises(Exception):
+        attention(*(torch.randn(1, 1, 64, 96, device=DEV) for _ in range(3)), precise=True)
