@@ -86,12 +86,21 @@ constexpr float kRescaleThreshold = 8.0f;
 #ifndef FA_ATTN_EMU2
 #define FA_ATTN_EMU2 1
 #endif
-// 1 = move registers from the producer/MMA warpgroup (56 per thread) to the
-// two softmax warpgroups (224 per thread) with setmaxnreg.  The split adds up
-// to the launch's 384 threads x 168 registers exactly.
+// 1 = move registers from the producer/MMA warpgroup (FA_ATTN_REGS_MMA per
+// thread) to the two softmax warpgroups (FA_ATTN_REGS_SOFTMAX) with
+// setmaxnreg.  128 x 56 + 256 x 224 is the launch's 384 threads x 168
+// registers exactly; any split must stay within that pool.
 #ifndef FA_ATTN_SETMAXNREG
 #define FA_ATTN_SETMAXNREG 1
 #endif
+#ifndef FA_ATTN_REGS_MMA
+#define FA_ATTN_REGS_MMA 56
+#endif
+#ifndef FA_ATTN_REGS_SOFTMAX
+#define FA_ATTN_REGS_SOFTMAX 224
+#endif
+static_assert(128 * FA_ATTN_REGS_MMA + 256 * FA_ATTN_REGS_SOFTMAX <= 384 * 168,
+              "register split exceeds the two-tile kernel's launch pool");
 // 1 = the attention kernels run persistent (one CTA per SM taking units from
 // a global counter) when there are more units than SMs, so a unit's Q and
 // first K/V tiles load, and its first S GEMMs run, while the previous unit
@@ -400,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp >= 8) {
     // Warpgroup 2: producer, MMA issuer, two idle warps.
 #if FA_ATTN_SETMAXNREG
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(FA_ATTN_REGS_MMA) : "memory");
 #endif
   if (warp == 8) {
     // =================== TMA producer ===================
@@ -600,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   } else {
 #if FA_ATTN_SETMAXNREG
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(FA_ATTN_REGS_SOFTMAX) : "memory");
 #endif
     // =================== softmax / correction / epilogue ===================
     const int t = warp >> 2;
@@ -647,17 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 1);
       if (j == 0 && t == 0 && lane == 0 && wq == 0) FA_CTA_TRACE(unit, 2, globaltimer_ns());
       uint32_t sr[128];
-      {
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        tmem_ld4x32_wait(tS, r0, r1, r2, r3);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          sr[i] = r0[i];
-          sr[32 + i] = r1[i];
-          sr[64 + i] = r2[i];
-          sr[96 + i] = r3[i];
-        }
-      }
+      tmem_ld128_wait(tS, sr);      // all 128 scores of the row, one tcgen05.ld
       const int k0 = j * kBN;
       const bool need_mask = (k0 + kBN > p.S) || (CAUSAL && (k0 + kBN - 1 > q_tile0));
       if (need_mask) {
