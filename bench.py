@@ -449,7 +449,7 @@ def sdpa_same_gpu(q, k, v, o, causal, flops_local, steps, warmup, world, device)
         tf = flops_local / (ms * 1e-3) / 1e12
         return {"value": tf, "unit": "TFLOP/s per GPU", "ms_per_step": ms,
                 "max_abs_diff_vs_ours": diff,
-                "what": "torch SDPA, cuDNN backend, same bf16 tensors, same event window"}
+                "what": "torch SDPA, cuDNN backend, same tensors, same event window"}
     except Exception as e:  # noqa: BLE001
         return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
 
@@ -552,6 +552,7 @@ def secondary_lines(args, fab, device, peaks):
                                                      cfg["causal"], flops, args.steps,
                                                      args.warmup, 1, device)
     del t, ref, err
+    out["legacy_fp16"] = legacy_fp16_line(args, fab, device, peaks)
     m = mlp_timing(args, fab, MLP_CONFIGS["cfg3"], MLP_CONFIGS["cfg3"]["M"], device, 1)
     out["cfg3"] = {"workload": "MLP block Y = gelu_tanh(X W1) W2, M=8192 K=4096 N=16384 bf16",
                    "value": m["value"], "unit": "TFLOP/s", "ms_per_step": m["ms"],
@@ -561,6 +562,40 @@ def secondary_lines(args, fab, device, peaks):
                    "clocks": m["clocks"], "gpu_launches": 2 * args.steps,
                    "verify": m["verify"]}
     return out
+
+
+def legacy_fp16_line(args, fab, device, peaks):
+    """The reference's legacy harness problem (old/benchmark.py:90-96): B8
+    S2048 H16 D64, fp16, non-causal, (B, S, H, D) tensors passed as strides;
+    device-timed like the headline, with torch SDPA (cuDNN) on the same
+    permuted tensors."""
+    B, S, H, D = 8, 2048, 16, 64
+    g = torch.Generator(device=device).manual_seed(7)
+    q, k, v = (torch.randn((B, S, H, D), generator=g, device=device).to(torch.float16)
+               for _ in range(3))
+    o = torch.empty_like(q)
+    ov = o.permute(0, 2, 1, 3)
+    qv, kv, vv = (t.permute(0, 2, 1, 3) for t in (q, k, v))
+    step = lambda: fab.attention(qv, kv, vv, out=ov)  # noqa: E731
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    with ClockSampler(local_index(device)) as clk:
+        ms = timed_loop(step, args.steps, 1, device)
+    flops = 4.0 * B * H * S * S * D
+    tf = flops / (ms * 1e-3) / 1e12
+    ref = torch_ref_pair(qv[0, 0], kv[0, 0], vv[0, 0], False)
+    err = (ov[0, 0].float() - ref).abs()
+    line = {"workload": "legacy harness: attention (B, S, H, D) = (8, 2048, 16, 64) fp16, "
+                        "non-causal, strided layout",
+            "value": tf, "unit": "TFLOP/s", "ms_per_step": ms, "dtype": "f16",
+            "roofline": roofline(tf, peaks, None), "clocks": clk.summary(),
+            "gpu_launches": args.steps,
+            "verify": {"pairs": 1, "max_abs": err.max().item(), "mean_abs": err.mean().item()}}
+    if not args.no_sdpa:
+        line["sdpa_same_gpu"] = sdpa_same_gpu(qv, kv, vv, ov, False, flops, args.steps,
+                                              args.warmup, 1, device)
+    return line
 
 
 def timed_gather(o, world, rank, device, reps=3):
