@@ -264,29 +264,30 @@ def attention_from_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if dev.type != "cuda":
         raise ValueError("device must be a CUDA device")
     for name, t in (("q", q), ("k", k), ("v", v)):
-        if t.is_cuda or t.dtype != _BF16:
-            raise ValueError(f"{name} must be a bfloat16 host tensor")
+        if t.is_cuda or t.dtype not in _HALF_TYPES or t.dtype != q.dtype:
+            raise ValueError(f"{name} must be a bfloat16 or float16 host tensor (all alike)")
         if t.dim() != 4 or not t.is_contiguous():
             raise ValueError(f"{name} must be a contiguous 4-D [B, H, S, D] tensor")
     B, H, S, D = q.shape
+    dtype = q.dtype
     pairs = B * H
     nch = max(1, min(int(chunks), pairs))
     bounds = [pairs * i // nch for i in range(nch + 1)]
     ws = workspace if workspace is not None else {}
-    key = (tuple(q.shape), dev, nch)
+    key = (tuple(q.shape), dtype, dev, nch)
     if ws.get("key") != key:
         for st in ws.get("streams", ()):
             st.synchronize()          # the old buffers may still be in use
         ws.clear()
         ws["key"] = key
         for name in ("q", "k", "v", "o"):
-            ws[name] = torch.empty((1, pairs, S, D), dtype=_BF16, device=dev)
+            ws[name] = torch.empty((1, pairs, S, D), dtype=dtype, device=dev)
         ws["streams"] = [torch.cuda.Stream(device=dev) for _ in range(3)]
         ws["ev_in"] = [torch.cuda.Event() for _ in range(nch)]
         ws["ev_cmp"] = [torch.cuda.Event() for _ in range(nch)]
         ws["ev_out"] = torch.cuda.Event()
     if out is None:
-        out = torch.empty(q.shape, dtype=_BF16, pin_memory=True)
+        out = torch.empty(q.shape, dtype=dtype, pin_memory=True)
     s_in, s_cmp, s_out = ws["streams"]
     cur = torch.cuda.current_stream(dev)
     # the previous call's consumers of the buffers are ordered before us

@@ -15,7 +15,8 @@ import torch
 from conftest import assert_close
 import oracle
 from cs348k_fast_attention_grammar_b200 import (attention, attention_bshd, attention_f32,
-                                                device_status, gemm_act, mlp)
+                                                attention_from_host, device_status, gemm_act,
+                                                mlp)
 from cs348k_fast_attention_grammar_b200 import kernel_module
 
 pytestmark = pytest.mark.gpu
@@ -193,3 +194,11 @@ def test_fp32_split_2d_entry_kt_layout_and_kernel_module():
     assert torch.equal(o2, out)
     with pytest.raises(Exception):
         attention(*(torch.randn(1, 1, 64, 96, device=DEV) for _ in range(3)), precise=True)
+
+
+def test_fp16_from_host_matches_device_call():
+    q, k, v = (_rand((1, 3, 384, 64), 410 + i, torch.float16).pin_memory() for i in range(3))
+    o_host = attention_from_host(q, k, v, causal=True, device=DEV, chunks=2)
+    torch.cuda.synchronize()
+    o_dev = attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=True)
+    assert o_host.dtype == torch.float16 and torch.equal(o_host, o_dev.cpu())
