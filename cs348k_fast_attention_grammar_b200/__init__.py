@@ -3,11 +3,11 @@
 Public operators (all run the hand-written kernels of ``libfa_b200.so``
 through its C ABI, ``include/fa_b200.h``; there is no fallback path):
 
-    attention(q, k, v, causal=False, scale=None, out=None)   # [B, H, S, D] bf16
+    attention(q, k, v, causal=False, scale=None, out=None)   # [B, H, S, D] bf16/fp16/fp32, D 8..128
     attention_bshd(q, k, v, causal=False)                    # (B, S, H, D) layout
     attention_f32(q, k, v, k_transposed=False)               # 2-D fp32 [N, D] (fn(KT, Q, V))
     attention_from_host(q, k, v, causal=False, ...)          # pinned host tensors
-    mlp(x, w1, w2, act="gelu_tanh")                          # act(x@w1)@w2
+    mlp(x, w1, w2, act="gelu_tanh")                          # act(x@w1)@w2, bf16/fp16
     mlp_ln(x, w1, w2)                                        # LN(relu(x@w1)@w2 + x)
     gemm_act(a, b, act="none")                               # act(a@b)
 
