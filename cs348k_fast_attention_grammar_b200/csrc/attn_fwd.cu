@@ -77,6 +77,23 @@ constexpr float kRescaleThreshold = 8.0f;
 #ifndef FA_ATTN_SPLIT_P
 #define FA_ATTN_SPLIT_P 1
 #endif
+// 1 = softmax blocks after a row's first skip (D <= 64 kernel) or halve
+// (two-tile kernel) the block maximum: the exponentials run against the
+// running reference maximum, and a block whose row sum exceeds 2^64 (or is
+// not finite) in any row of the warp is redone with the maximum taken and O
+// rescaled.  Measured: D = 64 non-causal +5 %, causal equal; two-tile kernel
+// causal -6 %, non-causal equal, so it is on for D <= 64 only.
+#ifndef FA_ATTN_SPEC_MAX_D64
+#define FA_ATTN_SPEC_MAX_D64 1
+#endif
+#ifndef FA_ATTN_SPEC_MAX_D128
+#define FA_ATTN_SPEC_MAX_D128 0
+#endif
+// 1 = the D <= 64 kernel's speculative path reads its 64 scores with one
+// TMEM load instead of two (measured 1-2 % slower than two).
+#ifndef FA_ATTN_SPEC_LD2
+#define FA_ATTN_SPEC_LD2 0
+#endif
 // Paired fp32 ops in the exponential loop: bit 0 = scale-and-subtract as one
 // fma.f32x2 per two scores, bit 1 = row sums accumulated with add.f32x2.
 #ifndef FA_ATTN_F2
@@ -136,7 +153,15 @@ __device__ __forceinline__ float exp2_fma(float x) {
 // floating-point ones paired (add.f32x2 / fma.f32x2; x - j as an exactly
 // rounded fma with -1), so an emulated pair costs 12 instructions instead
 // of 18.
+// HI_CLAMP also clamps x to <= 126 (for callers whose x may exceed the
+// exponent range, so that a huge x gives a huge result instead of a wrapped
+// exponent field).
+template <bool HI_CLAMP = false>
 __device__ __forceinline__ void exp2_fma_x2(float x0, float x1, float& r0, float& r1) {
+  if (HI_CLAMP) {
+    x0 = fminf(x0, 126.f);
+    x1 = fminf(x1, 126.f);
+  }
   const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
   const uint64_t t = fadd2(x, f2_pack(12582912.f, 12582912.f));
   const uint64_t j = fadd2(t, f2_pack(-12582912.f, -12582912.f));
@@ -340,6 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // error ~2^-22): the FMA-pipe polynomial's 7.5e-5 would dominate its error.
   constexpr int kEmuMod = SPLIT ? 0 : (D == 64) ? FA_ATTN_EMU_MOD_D64 : FA_ATTN_EMU_MOD_D128;
   constexpr bool kPackAlu = FA_ATTN_PACK_ALU != 0 && !F16;
+  constexpr bool kSpec = FA_ATTN_SPEC_MAX_D128 != 0 && !SPLIT;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -665,45 +691,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < kBN; ++c)
           if (k0 + c >= lim) sr[c] = __float_as_uint(-INFINITY);
       }
-      // Row max as four independent chains of 3-input maxima (short latency).
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int c = 0; c < kBN; c += 8)
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          mx4[i] = fmax3(mx4[i], __uint_as_float(sr[c + 2 * i]), __uint_as_float(sr[c + 2 * i + 1]));
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      const float m_blk = mx * sl2;
-      const float m_new = fmaxf(m_ref, m_blk);
-      const bool need = (m_new - m_ref) > kRescaleThreshold;
-      if (__any_sync(0xffffffffu, need)) {
-        const float m_use = need ? m_new : m_ref;
-        const float alpha = ex2_approx(m_ref - m_use);   // 1 if unchanged, 0 at start
-        if (j > 0) {
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32_wait(tO + c * 32, o);
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(tO + c * 32, o);
-          }
-        }
-        l *= alpha;
-        m_ref = m_use;
-      }
-      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 2);
-      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 3);
-      const float neg_m = -m_ref;
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
       uint64_t rs2[2] = {0ull, 0ull};
       const uint64_t sl2x2 = f2_pack(sl2, sl2);
-      const uint64_t negm2 = f2_pack(neg_m, neg_m);
       uint32_t pk[2][32];
       uint32_t pl[2][32];    // SPLIT: bf16 remainders of the probabilities
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      // Exponentials of one half of the row (keys 64 half .. 64 half + 63)
+      // against the reference -neg_m: packed P into pk[half], sums into rs / rs2.
+      auto exp_half = [&](int half, float neg_m) {
+        const uint64_t negm2 = f2_pack(neg_m, neg_m);
 #pragma unroll
         for (int cc = 0; cc < 32; ++cc) {
           const int c = half * 32 + cc;
@@ -721,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool emu = (kEmuMod > 0) && (c % (kEmuMod > 0 ? kEmuMod : 1) == kEmuMod - 1);
           float p0, p1;
           if (emu && FA_ATTN_EMU2) {
-            exp2_fma_x2(x0, x1, p0, p1);
+            exp2_fma_x2<kSpec>(x0, x1, p0, p1);
           } else {
             p0 = emu ? exp2_fma(x0) : ex2_approx(x0);
             p1 = emu ? exp2_fma(x1) : ex2_approx(x1);
@@ -735,24 +731,81 @@ __global__ void __launch_bounds__(kThreads, 1)
             pl[half][cc] = pack_bf16x2(p0 - __uint_as_float(pk[half][cc] << 16),
                                        p1 - __uint_as_float(pk[half][cc] & 0xffff0000u));
         }
-        if (FA_ATTN_SPLIT_P && half == 0) {
-          // keys 0-63 of P -> TMEM columns [0, 32); the MMA warp starts on them
-          tmem_st32(tS, pk[0]);
-          if (SPLIT) tmem_st32(tS + 64, pl[0]);
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(bar_p_half(t));
-        }
-      }
-      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 4);
-      if (FA_ATTN_F2 & 2) {
+      };
+      auto row_sum = [&]() {
         float a0, a1, b0, b1;
         f2_unpack(rs2[0], a0, a1);
         f2_unpack(rs2[1], b0, b1);
-        l += (a0 + a1) + (b0 + b1);
-      } else {
-        l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+        return ((a0 + a1) + (b0 + b1)) + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+      };
+      // Speculative path (every block after the first): the first half is
+      // exponentiated against the running reference maximum while only the
+      // second half's maximum is taken; both are kept if every row's first
+      // half sums to <= 2^64 and its second half's maximum is within 64
+      // (log2 units) of the reference (2^15 and 8 for fp16 P), else the block
+      // is redone the exact way below (all scores are still in registers).
+      bool fast = kSpec && __all_sync(0xffffffffu, m_ref != -INFINITY);
+      if (fast) {
+        float h4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = kBN / 2; c < kBN; c += 8)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            h4[i] = fmax3(h4[i], __uint_as_float(sr[c + 2 * i]), __uint_as_float(sr[c + 2 * i + 1]));
+        exp_half(0, -m_ref);
+        const float m_h1 = fmaxf(fmaxf(h4[0], h4[1]), fmaxf(h4[2], h4[3])) * sl2;
+        fast = __all_sync(0xffffffffu, row_sum() <= (F16 ? 0x1p15f : 0x1p64f) &&
+                                           m_h1 - m_ref <= (F16 ? 8.f : 64.f));
+        if (!fast) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) rs[i] = 0.f;
+          rs2[0] = rs2[1] = 0ull;
+        }
       }
+      if (!fast) {
+        // Row max as four independent chains of 3-input maxima (short latency).
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < kBN; c += 8)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            mx4[i] = fmax3(mx4[i], __uint_as_float(sr[c + 2 * i]), __uint_as_float(sr[c + 2 * i + 1]));
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        const float m_blk = mx * sl2;
+        const float m_new = fmaxf(m_ref, m_blk);
+        const bool need = (m_new - m_ref) > kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_use = need ? m_new : m_ref;
+          const float alpha = ex2_approx(m_ref - m_use);   // 1 if unchanged, 0 at start
+          if (j > 0) {
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32_wait(tO + c * 32, o);
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st32(tO + c * 32, o);
+            }
+          }
+          l *= alpha;
+          m_ref = m_use;
+        }
+        if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 2);
+        exp_half(0, -m_ref);
+      }
+      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 3);
+      if (FA_ATTN_SPLIT_P) {
+        // keys 0-63 of P -> TMEM columns [0, 32); the MMA warp starts on them
+        tmem_st32(tS, pk[0]);
+        if (SPLIT) tmem_st32(tS + 64, pl[0]);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_p_half(t));
+      }
+      exp_half(1, -m_ref);
+      if (lane == 0 && wq == 0) FA_TRACE(j, 6 * t + 4);
+      l += row_sum();
       if (!FA_ATTN_SPLIT_P) tmem_st32(tS, pk[0]);
       if (!FA_ATTN_SPLIT_P && SPLIT) tmem_st32(tS + 64, pl[0]);
       tmem_st32(tS + 32, pk[1]);
@@ -908,6 +961,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
   constexpr int D = 64;
   constexpr int kNT = 4;
   constexpr int kEmuMod = FA_ATTN_EMU_MOD_D64;
+  constexpr bool kSpec = FA_ATTN_SPEC_MAX_D64 != 0;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -1155,57 +1209,18 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
       const int k0 = j * kQ4BN;
       const bool need_mask = (k0 + kQ4BN > p.S) || (CAUSAL && (k0 + kQ4BN - 1 > q_tile0));
       const int lim = CAUSAL ? min(qi + 1, p.S) : p.S;
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        uint32_t r[32];
-        tmem_ld32_wait(tS + 32 * ch, r);
-        if (need_mask) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (k0 + 32 * ch + c >= lim) r[c] = __float_as_uint(-INFINITY);
-        }
-#pragma unroll
-        for (int c = 0; c < 32; c += 8)
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            mx4[i] = fmax3(mx4[i], __uint_as_float(r[c + 2 * i]), __uint_as_float(r[c + 2 * i + 1]));
-      }
-      const float m_blk = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
-      const bool need = (m_ref == -INFINITY) ? (m_blk > -INFINITY)
-                                             : (m_blk - m_ref > kRescaleThreshold);
-      if (__any_sync(0xffffffffu, need)) {
-        const float m_use = need ? m_blk : m_ref;
-        const float alpha = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - m_use);
-        if (j > 0) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t o[32];
-            tmem_ld32_wait(tO + c * 32, o);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(tO + c * 32, o);
-          }
-          tmem_wait_st();
-        }
-        l *= alpha;
-        m_ref = m_use;
-      }
-      if (lane == 0 && wq == 0) FA_TRACE(j, 4 * t + 2);
-      const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
       const uint64_t sl2x2 = f2_pack(sl2, sl2);
-      const uint64_t negm2 = f2_pack(neg_m, neg_m);
-      uint64_t rs2[2] = {0ull, 0ull};
-#pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        uint32_t r[32];
-        tmem_ld32_wait(tS + 32 * ch, r);
+      // Exponentials of one 32-column chunk of S against reference neg_m:
+      // packed probabilities into pk, row sums into rs2.
+      // exp_vals: the same for 32 scores already in registers.
+      auto exp_vals = [&](uint32_t* r, int ch, float neg_m, uint32_t (&pk)[16],
+                          uint64_t (&rs2)[2]) {
         if (need_mask) {
 #pragma unroll
           for (int c = 0; c < 32; ++c)
             if (k0 + 32 * ch + c >= lim) r[c] = __float_as_uint(-INFINITY);
         }
-        uint32_t pk[16];
+        const uint64_t negm2 = f2_pack(neg_m, neg_m);
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           float x0, x1;
@@ -1216,7 +1231,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
           const bool emu = (kEmuMod > 0) && (pair % (kEmuMod > 0 ? kEmuMod : 1) == kEmuMod - 1);
           float p0, p1;
           if (emu) {
-            exp2_fma_x2(x0, x1, p0, p1);
+            exp2_fma_x2<kSpec>(x0, x1, p0, p1);
           } else {
             p0 = ex2_approx(x0);
             p1 = ex2_approx(x1);
@@ -1224,16 +1239,98 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
           rs2[c & 1] = fadd2(rs2[c & 1], f2_pack(p0, p1));
           pk[c] = pack_16x2<F16>(p0, p1);
         }
-        tmem_st16(tS + 16 * ch, pk);
+      };
+      auto exp_chunk = [&](int ch, float neg_m, uint32_t (&pk)[16], uint64_t (&rs2)[2]) {
+        uint32_t r[32];
+        tmem_ld32_wait(tS + 32 * ch, r);
+        exp_vals(r, ch, neg_m, pk, rs2);
+      };
+      auto sum2 = [](const uint64_t (&rs2)[2]) {
+        float a0, a1, b0, b1;
+        f2_unpack(rs2[0], a0, a1);
+        f2_unpack(rs2[1], b0, b1);
+        return (a0 + a1) + (b0 + b1);
+      };
+      float l_blk = 0.f;
+      // Speculative path (every block after a row's first): exponentiate
+      // against the running reference maximum without taking the block
+      // maximum; keep the result only if every row's block sum stays <= 2^64
+      // (finite, far from fp32 overflow; 2^15 for fp16 P), else take the
+      // exact path below.
+      bool fast = kSpec && __all_sync(0xffffffffu, m_ref != -INFINITY);
+      if (fast) {
+        uint32_t pk0[16], pk1[16];
+        uint64_t rs2[2] = {0ull, 0ull};
+        if (FA_ATTN_SPEC_LD2) {
+          uint32_t r[64];
+          tmem_ld64_wait(tS, r);
+          exp_vals(r, 0, -m_ref, pk0, rs2);
+          exp_vals(r + 32, 1, -m_ref, pk1, rs2);
+        } else {
+          exp_chunk(0, -m_ref, pk0, rs2);
+          exp_chunk(1, -m_ref, pk1, rs2);
+        }
+        l_blk = sum2(rs2);
+        // (fp16 P: every probability must stay below fp16's 65504)
+        fast = __all_sync(0xffffffffu, l_blk <= (F16 ? 0x1p15f : 0x1p64f));
+        if (fast) {
+          tmem_st16(tS, pk0);
+          tmem_st16(tS + 16, pk1);
+        }
+      }
+      if (!fast) {
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          uint32_t r[32];
+          tmem_ld32_wait(tS + 32 * ch, r);
+          if (need_mask) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (k0 + 32 * ch + c >= lim) r[c] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int c = 0; c < 32; c += 8)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              mx4[i] = fmax3(mx4[i], __uint_as_float(r[c + 2 * i]), __uint_as_float(r[c + 2 * i + 1]));
+        }
+        const float m_blk = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+        const bool need = (m_ref == -INFINITY) ? (m_blk > -INFINITY)
+                                               : (m_blk - m_ref > kRescaleThreshold);
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_use = need ? m_blk : m_ref;
+          const float alpha = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - m_use);
+          if (j > 0) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              uint32_t o[32];
+              tmem_ld32_wait(tO + c * 32, o);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st32(tO + c * 32, o);
+            }
+            tmem_wait_st();
+          }
+          l *= alpha;
+          m_ref = m_use;
+        }
+        if (lane == 0 && wq == 0) FA_TRACE(j, 4 * t + 2);
+        const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
+        uint64_t rs2[2] = {0ull, 0ull};
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          uint32_t pk[16];
+          exp_chunk(ch, neg_m, pk, rs2);
+          tmem_st16(tS + 16 * ch, pk);
+        }
+        l_blk = sum2(rs2);
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_p_full(t));
       if (lane == 0 && wq == 0) FA_TRACE(j, 4 * t + 3);
-      float a0, a1, b0, b1;
-      f2_unpack(rs2[0], a0, a1);
-      f2_unpack(rs2[1], b0, b1);
-      l += (a0 + a1) + (b0 + b1);
+      l += l_blk;
     }
     if (ok && my_nt > 0 && wwait(bar_o_full(t), ou & 1)) {
       tc_fence_after();

@@ -334,3 +334,26 @@ def test_persistent_launches_on_two_streams():
             bad[s] += int(not torch.equal(outs[s], want[s]))
     assert bad == [0, 0]
     assert device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [32, 64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_score_jump_in_later_block(dtype, D, causal):
+    """A key in a later key block scores far above everything before it for
+    some rows (more than 64 in log2 units, beyond the range the softmax keeps
+    against its running reference maximum), so those rows take the exact
+    path: block maximum, O rescaled, probabilities redone.  Other rows of the
+    same warps stay on the fast path.  Checked against the fp64 oracle."""
+    S = 512
+    g = torch.Generator().manual_seed(400 + D + int(causal))
+    q, k, v = (torch.randn((1, 2, S, D), generator=g) for _ in range(3))
+    q[:, :, 320:400] = 3.0          # these rows ...
+    k[:, :, 300] = 3.0              # ... meet this key in key block 2 (or 4)
+    k[:, 1, 450] = 2.0              # a smaller jump in head 1
+    q, k, v = (t.to(dtype) for t in (q, k, v))
+    out = attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    torch.cuda.synchronize()
+    ref = oracle.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), causal=causal)
+    assert_close(out.float().cpu().numpy(), ref, what=f"{dtype} D{D} causal={causal}")
+    assert device_status() == 0
