@@ -183,12 +183,19 @@ def timed_loop(fn, steps: int, world: int, device) -> float:
     t1.record(stream)
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1) / steps
+    LAST_RANK_MS.update(min=ms, max=ms)
     if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        t = torch.tensor([ms, -ms], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
+        ms = t[0].item()
+        LAST_RANK_MS.update(min=-t[1].item(), max=ms)
         dist.barrier()
     return ms
+
+
+# Fastest and slowest rank of the last timed_loop (the reported time is the
+# slowest); the spread shows whether one GPU or all of them set the time.
+LAST_RANK_MS = {"min": 0.0, "max": 0.0}
 
 
 def max_over_ranks(x: float, world: int, device) -> float:
@@ -426,8 +433,10 @@ def attention_timing(args, fab, cfg, pairs, device, world, steps, warmup):
     torch.cuda.synchronize()
     with ClockSampler(local_index(device)) as clk:
         ms = timed_loop(step, steps, world, device)
+    rank_ms = dict(LAST_RANK_MS)
     reps = timed_reps(step, 5, world, device)
-    return {"q": q, "k": k, "v": v, "o": o, "ms": ms, "reps": reps, "clocks": clk.summary()}
+    return {"q": q, "k": k, "v": v, "o": o, "ms": ms, "reps": reps, "clocks": clk.summary(),
+            "rank_ms": rank_ms}
 
 
 def sdpa_same_gpu(q, k, v, o, causal, flops_local, steps, warmup, world, device):
@@ -478,6 +487,7 @@ def bench_attention(args, fab, device, world, rank):
                              load_traffic(args.config) if args.pairs <= 0 else None),
         "gpu_launches": args.steps,
         "clocks": t["clocks"],
+        "rank_ms_per_step": {"fastest": t["rank_ms"]["min"], "slowest": t["rank_ms"]["max"]},
         "flops_per_step": flops_total,
         "flop_convention": "4*B*H*S^2*D, halved when causal (old/benchmark.py:131)",
     }

@@ -125,6 +125,11 @@ static_assert(128 * FA_ATTN_REGS_MMA + 256 * FA_ATTN_REGS_SOFTMAX <= 384 * 168,
 #ifndef FA_ATTN_PERSIST
 #define FA_ATTN_PERSIST 1
 #endif
+// 1 = the last partial wave of equal four-tile units runs as half units
+// (see AttnParams::split_from).
+#ifndef FA_ATTN_SPLIT_TAIL
+#define FA_ATTN_SPLIT_TAIL 1
+#endif
 // Counter pairs for persistent launches, handed out round-robin per launch.
 constexpr int kUnitCtrSlots = 1024;
 __device__ unsigned int g_attn_unit_ctr[2 * kUnitCtrSlots];
@@ -235,6 +240,11 @@ struct AttnParams {
   // 128-row Q tiles per work unit: the kernel's full width (2 or 4), or
   // fewer for small problems so that more SMs get a unit.
   int tiles_per_unit;
+  // Four-tile kernel: units from split_from on are halves (tiles_per_unit / 2
+  // tiles) of the units split_from, split_from + 1, ..., two per unit, so a
+  // last partial wave of equal units runs on twice as many SMs.
+  // split_from >= total_units: no split.
+  int split_from;
 };
 
 // Optional timeline instrumentation (compiled out unless FA_ATTN_TRACE):
@@ -921,6 +931,12 @@ struct AttnQ4Cfg {
 template <bool CAUSAL>
 __device__ __forceinline__ void decode_unit_q4(const AttnParams& p, int unit, int& b, int& h,
                                                int& q0, int nt[4]) {
+  int half = -1;
+  if (unit >= p.split_from) {
+    const int x = unit - p.split_from;
+    unit = p.split_from + (x >> 1);
+    half = x & 1;
+  }
   int heads_here, first_bh, r_in;
   const int big_units = (p.group_q + 1) * p.n_units_per_head;
   const int big_span = p.group_r * big_units;
@@ -943,10 +959,15 @@ __device__ __forceinline__ void decode_unit_q4(const AttnParams& p, int unit, in
   b = bh / p.H;
   h = bh - b * p.H;
   q0 = qu * p.tiles_per_unit * kBM;
+  int tpu = p.tiles_per_unit;
+  if (half >= 0) {
+    tpu >>= 1;
+    q0 += half * tpu * kBM;
+  }
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
     const int qs = q0 + t * kBM;
-    if (t >= p.tiles_per_unit || qs >= p.S) nt[t] = 0;
+    if (t >= tpu || qs >= p.S) nt[t] = 0;
     else if (CAUSAL) nt[t] = min(p.nkv, (qs + kBM - 1) / kQ4BN + 1);
     else nt[t] = p.nkv;
   }
@@ -1489,8 +1510,21 @@ int run_attn(const void* q, const void* k, const void* v, void* o, int B, int H,
   prm.total_units = grid;
   prm.unit_ctr = nullptr;
   prm.tiles_per_unit = tpu;
+  prm.split_from = prm.total_units;
   if (FA_ATTN_PERSIST && grid > sms) {
     prm.unit_ctr = ctr;
+    // Equal-length units (four-tile kernel, non-causal) leave a last partial
+    // wave of r units on r SMs; when 2r SMs are available those units run
+    // as 2r half units instead (B8 H16 S2048 D64: 512 units = 3 waves + 68).
+    // Both halves of a split unit must hold rows: each head's last unit
+    // (where the schedule ends) is full or more than half full.
+    const int r = prm.total_units % sms;
+    const int rem = S % unit_rows;
+    if (FA_ATTN_SPLIT_TAIL && q4 && !causal && tpu == 4 && r > 0 && 2 * r <= sms &&
+        (rem == 0 || 2 * rem > unit_rows)) {
+      prm.split_from = prm.total_units - r;
+      prm.total_units += r;
+    }
     grid = sms;
   }
   if (q4) {

@@ -357,3 +357,18 @@ def test_score_jump_in_later_block(dtype, D, causal):
     ref = oracle.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), causal=causal)
     assert_close(out.float().cpu().numpy(), ref, what=f"{dtype} D{D} causal={causal}")
     assert device_status() == 0
+
+
+@pytest.mark.parametrize("S", [1024, 1000])
+def test_split_last_wave_matches_oracle(S):
+    """Non-causal D = 64 with a last partial wave of r <= SMs / 2 equal units:
+    those units run as half units (two per unit).  S = 1024 fills every unit,
+    S = 1000 leaves each head's last unit 488 of 512 rows.  Every head is
+    checked against the oracle."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    H = (sms + 12) // 2                  # 2 units per head: units = sms + 12 (or 11)
+    q, k, v = (_rand((1, H, S, 64), 90 + i) for i in range(3))
+    out = _run(q, k, v, False)
+    ref = oracle.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), causal=False)
+    assert_close(out, ref, what=f"split tail S={S} H={H}")
+    assert device_status() == 0
