@@ -183,14 +183,20 @@ def timed_loop(fn, steps: int, world: int, device) -> float:
     t1.record(stream)
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1) / steps
-    LAST_RANK_MS.update(min=ms, max=ms)
+    slowest, fastest = rank_ms_spread(ms, world, device)
+    LAST_RANK_MS.update(min=fastest, max=slowest)
     if world > 1:
-        t = torch.tensor([ms, -ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t[0].item()
-        LAST_RANK_MS.update(min=-t[1].item(), max=ms)
         dist.barrier()
-    return ms
+    return slowest
+
+
+def rank_ms_spread(ms: float, world: int, device) -> tuple:
+    """(slowest, fastest) of every rank's ``ms`` (one all-reduce)."""
+    if world == 1:
+        return ms, ms
+    t = torch.tensor([ms, -ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t[0].item(), -t[1].item()
 
 
 # Fastest and slowest rank of the last timed_loop (the reported time is the

@@ -149,3 +149,26 @@ def test_two_gloo_ranks_mlp_row_split_matches_single_process(tmp_path):
     assert res["y"].shape == (MLP_CFG["M"], MLP_CFG["K"])
     np.testing.assert_array_equal(res["y"].numpy(), single)
     assert res["stats"]["max_abs"] == 0.0 and res["stats"]["elements"] == 2 * 8 * MLP_CFG["K"]
+
+
+def _spread_worker(rank, world, port, result_path):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=30))
+    try:
+        got = bench.rank_ms_spread(1.0 + rank, world, "cpu")
+        torch.save(got, f"{result_path}.{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bench_rank_spread_on_two_gloo_ranks(tmp_path):
+    """bench.py's step time is the slowest rank's; the line also reports the
+    fastest.  Every rank gets both from one all-reduce."""
+    out = str(tmp_path / "spread")
+    mp.spawn(_spread_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    for r in range(2):
+        assert torch.load(f"{out}.{r}") == (2.0, 1.0)
