@@ -909,15 +909,23 @@ int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
 constexpr int kQ4Threads = 640;
 constexpr int kQ4BN = 64;
 
+// 1 = the four-tile kernel's ring slots hold a K block and the V block of
+// the same keys (16 KiB, 8 slots): one wait and one release per key block in
+// the MMA thread instead of two of each; 0 = K and V in separate 8 KiB slots.
+#ifndef FA_ATTN_Q4_KVPAIR
+#define FA_ATTN_Q4_KVPAIR 1
+#endif
 struct AttnQ4Cfg {
   static constexpr int kTileBytes = kBM * 64 * 2;          // Q tile, 16 KiB
   static constexpr int kKVBytes = kQ4BN * 64 * 2;          // K or V block, 8 KiB
-  static constexpr int kStages = 16;
+  static constexpr bool kPair = FA_ATTN_Q4_KVPAIR != 0;
+  static constexpr int kSlotBytes = kPair ? 2 * kKVBytes : kKVBytes;
+  static constexpr int kStages = kPair ? 8 : 16;
   static constexpr int kQOff = 0;
   static constexpr int kKVOff = 4 * kTileBytes;
-  static constexpr int kBarOff = kKVOff + kStages * kKVBytes;
-  // q, kv_full[16], kv_empty[16], s_full[4], p_full[4], o_full[4], drain,
-  // q_empty, unit_full[2], unit_empty[2]
+  static constexpr int kBarOff = kKVOff + kStages * kSlotBytes;
+  // q, kv_full[kStages], kv_empty[kStages], s_full[4], p_full[4], o_full[4],
+  // drain, q_empty, unit_full[2], unit_empty[2]
   static constexpr int kNumBars = 1 + 2 * kStages + 12 + 1 + 5;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
@@ -1078,18 +1086,25 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
             tma_load_4d(sQ + t * C::kTileBytes, &tmQ, bar_q, 0, q0 + t * kBM, h, b, pol_q);
         ++uc;
         bool kv_ok = true;
-        for (int i = 0; i < 2 * n; ++i) {
+        for (int i = 0; i < (C::kPair ? n : 2 * n); ++i) {
           const int s = issued % C::kStages;
           const uint32_t ph = (issued / C::kStages) & 1;
           if (!mbar_wait(bar_kv_empty(s), ph ^ 1u, abort_flag, p.status)) {
             kv_ok = false;
             break;
           }
-          mbar_arrive_expect_tx(bar_kv_full(s), C::kKVBytes);
-          const void* map = (i & 1) ? static_cast<const void*>(&tmV)
-                                    : static_cast<const void*>(&tmK);
-          tma_load_4d(sKV + s * C::kKVBytes, map, bar_kv_full(s), 0, (i >> 1) * kQ4BN, h, b,
-                      pol_kv);
+          mbar_arrive_expect_tx(bar_kv_full(s), C::kSlotBytes);
+          if (C::kPair) {
+            // K_i at the slot's start, V_i 8 KiB after it
+            tma_load_4d(sKV + s * C::kSlotBytes, &tmK, bar_kv_full(s), 0, i * kQ4BN, h, b, pol_kv);
+            tma_load_4d(sKV + s * C::kSlotBytes + C::kKVBytes, &tmV, bar_kv_full(s), 0,
+                        i * kQ4BN, h, b, pol_kv);
+          } else {
+            const void* map = (i & 1) ? static_cast<const void*>(&tmV)
+                                      : static_cast<const void*>(&tmK);
+            tma_load_4d(sKV + s * C::kSlotBytes, map, bar_kv_full(s), 0, (i >> 1) * kQ4BN, h, b,
+                        pol_kv);
+          }
           ++issued;
         }
         if (!kv_ok) break;
@@ -1150,7 +1165,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t vbase = sKV + vslot * C::kKVBytes;
+            const uint32_t vbase = sKV + vslot * C::kSlotBytes + (C::kPair ? C::kKVBytes : 0);
 #pragma unroll
             for (int kk = 0; kk < kQ4BN / 16; ++kk) {
               const uint64_t bdesc = sdesc_sw128(vbase + kk * 2048, kQ4BN * 128, 1024);
@@ -1161,7 +1176,7 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
           }
           if (j < nt[t]) {
             const uint32_t qbase = sQ + t * C::kTileBytes;
-            const uint32_t kbase = sKV + kslot * C::kKVBytes;
+            const uint32_t kbase = sKV + kslot * C::kSlotBytes;
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk)
               mma_ss(tmem + C::col_s(t), sdesc_sw128(qbase + kk * 32, 16, 1024),
@@ -1170,6 +1185,15 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
           }
         }
         if (!ok) break;
+        if (C::kPair) {
+          // The slot of block j - 1 (K used by S(j - 1), V by the P V just
+          // issued) is free once these MMAs complete; block j's slot serves
+          // the next iteration's P V.
+          if (j >= 1) mma_commit(bar_kv_empty(vslot));
+          if (j == n - 1) mma_commit(bar_q_empty);        // the unit's last S GEMMs
+          vslot = kslot;
+          continue;
+        }
         if (j >= 1) mma_commit(bar_kv_empty(vslot));
         if (j < n) {
           mma_commit(bar_kv_empty(kslot));
