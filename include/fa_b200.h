@@ -91,7 +91,8 @@ int fa_version(void);
  *   stream     : cudaStream_t (NULL = legacy default stream).
  * Computes in fp32 (tcgen05 bf16 MMAs with fp32 accumulation in TMEM).
  * With more work units (256 query rows at D = 128, 512 at D = 64; fewer
- * rows when the problem would leave most SMs idle) than SMs
+ * rows when the problem would leave most SMs idle, and at D <= 64 without a
+ * causal mask a last partial wave of units split into halves) than SMs
  * the kernel runs persistent and takes units from one of 1024 library-owned
  * device counters, handed out round-robin per call and reset by the launch
  * that used it; a counter is shared only if 1024 further calls are issued
