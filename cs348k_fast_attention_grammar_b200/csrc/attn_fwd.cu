@@ -915,6 +915,21 @@ constexpr int kQ4BN = 64;
 #ifndef FA_ATTN_Q4_KVPAIR
 #define FA_ATTN_Q4_KVPAIR 1
 #endif
+// 1 = the four-tile kernel moves registers from warpgroup 4 (producer, MMA
+// issuer, two idle warps: FA_ATTN_Q4_REGS_CTRL each) to the 16 softmax warps
+// (FA_ATTN_Q4_REGS_SOFTMAX each).  The launch holds 640 threads x 96
+// registers (five warps per sub-partition); any split must stay within it.
+#ifndef FA_ATTN_Q4_SETMAXNREG
+#define FA_ATTN_Q4_SETMAXNREG 0
+#endif
+#ifndef FA_ATTN_Q4_REGS_CTRL
+#define FA_ATTN_Q4_REGS_CTRL 40
+#endif
+#ifndef FA_ATTN_Q4_REGS_SOFTMAX
+#define FA_ATTN_Q4_REGS_SOFTMAX 104
+#endif
+static_assert(128 * FA_ATTN_Q4_REGS_CTRL + 512 * FA_ATTN_Q4_REGS_SOFTMAX <= 640 * 96,
+              "register split exceeds the four-tile kernel's launch pool");
 struct AttnQ4Cfg {
   static constexpr int kTileBytes = kBM * 64 * 2;          // Q tile, 16 KiB
   static constexpr int kKVBytes = kQ4BN * 64 * 2;          // K or V block, 8 KiB
@@ -1052,6 +1067,11 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp >= 16) {
+    // Warpgroup 4: producer, MMA issuer, two idle warps.
+#if FA_ATTN_Q4_SETMAXNREG
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(FA_ATTN_Q4_REGS_CTRL) : "memory");
+#endif
   if (warp == 16) {
     // =================== TMA producer ===================
     if (elect_one()) {
@@ -1214,7 +1234,11 @@ __global__ void __launch_bounds__(kQ4Threads, 1)
       drain_wait(bar_drain, 0);
     }
     __syncwarp();
-  } else if (warp < 16) {
+  }
+  } else {
+#if FA_ATTN_Q4_SETMAXNREG
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(FA_ATTN_Q4_REGS_SOFTMAX) : "memory");
+#endif
     // =================== softmax / epilogue (one tile) ===================
     const int t = warp >> 2;
     const int wq = warp & 3;
