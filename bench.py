@@ -65,6 +65,9 @@ def parse_args(argv=None):
                     help="skip the cfg1 / cfg3 lines of the default single-GPU run")
     ap.add_argument("--no-sdpa", action="store_true",
                     help="skip the same-GPU torch SDPA (cuDNN) comparator")
+    ap.add_argument("--sdpa-only", action="store_true",
+                    help="attention configs: time only the torch SDPA (cuDNN) comparator on "
+                         "the same seeded tensors (a profiler run of the library kernel)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="(batch, head) chunks pipelined over the copy/kernel streams")
@@ -473,6 +476,15 @@ def bench_attention(args, fab, device, world, rank):
     cfg = ATTN_CONFIGS[args.config]
     num_pairs = cfg["B"] * cfg["H"] if args.pairs <= 0 else min(args.pairs, cfg["B"] * cfg["H"])
     pairs = shard_range(num_pairs, world, rank)
+    if args.sdpa_only:
+        q, k, v = make_qkv(cfg, pairs, device)
+        o = torch.empty_like(q)
+        flops_local = attn_flops(cfg, len(pairs))
+        r = sdpa_same_gpu(q, k, v, o, cfg["causal"], flops_local, args.steps, args.warmup,
+                          world, device)
+        return {"metric": METRIC, "impl": "torch SDPA (cuDNN) comparator", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup,
+                "config": workload_config(args, cfg, num_pairs), "sdpa_same_gpu": r}
     t = attention_timing(args, fab, cfg, pairs, device, world, args.steps, args.warmup)
     q, k, v, o, ms = t["q"], t["k"], t["v"], t["o"], t["ms"]
     flops_total = attn_flops(cfg, num_pairs)
